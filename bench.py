@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Benchmark of the NVFP4 GEMM hot path (BASELINE.json metric: NVFP4 GEMM TFLOPS at
+4096x14336x4096 and % of the measured tcgen05 FP4 peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--config c2|c1|c3|decode-up-16|...]
+
+One step = one D = A*B^T launch of the workload (config 2 of BASELINE.json by default:
+M=4096 tokens, N=14336, K=4096, N(0,1) operands quantised on the GPU to E2M1/UE4M3, BF16 out).
+Under torchrun every rank computes its own N-slice of a problem N*world wide (weak scaling,
+no data-path collective). Rank 0 prints one JSON line.
+
+`value` is device-timed: operands resident in HBM, L2 flushed (256 MiB write) before every
+step, CUDA events around each launch on the launching stream, max over ranks. `e2e` is the
+same metric through the C ABI with pinned host buffers: each step copies the quantised
+operands host->device, launches, and copies C device->host, all inside the timed region.
+`--impl reference` times the reference's own algorithm for this path on the host cores (the
+CPU restatement of src/reference.cu in oracle/, over dequantised operands) on a bounded
+sample of output rows; it never touches the GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (M, N, K, out dtype, description)
+    "c1": (1024, 1024, 1024, "f32", "NVFP4 GEMM 1024^3, FP32 out (BASELINE config 1)"),
+    "c2": (4096, 14336, 4096, "bf16", "LLM FFN up-proj 4096x14336x4096, BF16 out (BASELINE config 2)"),
+    "c3": (8192, 8192, 8192, "bf16", "square 8192^3, BF16 out (BASELINE config 3, 1 GPU)"),
+    "decode-up-16": (16, 14336, 4096, "bf16", "decode M=16 up-proj"),
+    "decode-up-64": (64, 14336, 4096, "bf16", "decode M=64 up-proj"),
+    "decode-up-128": (128, 14336, 4096, "bf16", "decode M=128 up-proj"),
+    "decode-down-16": (16, 4096, 14336, "bf16", "decode M=16 down-proj"),
+    "decode-down-64": (64, 4096, 14336, "bf16", "decode M=64 down-proj"),
+    "decode-down-128": (128, 4096, 14336, "bf16", "decode M=128 down-proj"),
+}
+SEED_A, SEED_B = 1234, 1234 ^ 0xABCDEF
+
+
+def algorithmic_bytes(M, N, K, out_bytes):
+    """Operand values + scales read once, C written once (SURVEY roofline convention)."""
+    return M * K / 2 + M * K / 16 + N * K / 2 + N * K / 16 + M * N * out_bytes
+
+
+# ------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks, power, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------- reference arm
+def cpu_reference_sample(M, N, K, target_s, threads=0):
+    """Time the oracle (CPU restatement of src/reference.cu:9-17) on a seeded sample of
+    output rows of the workload: returns (tflops, rows, seconds, threads)."""
+    import oracle
+    rng = np.random.default_rng(SEED_A)
+    # Host operands of the workload's shape: uniform fill (src/nvfp4.cu:115-129) quantised and
+    # dequantised by the oracle, exactly the values the reference's oracle consumes.
+    a_rows = 64
+    a = oracle.make_uniform(a_rows, K, SEED_A)
+    b = oracle.make_uniform(N, K, SEED_B)
+    pa, sa = oracle.quantize(a)
+    pb, sb = oracle.quantize(b)
+    adq = oracle.dequantize(pa, sa, K)
+    bdq = oracle.dequantize(pb, sb, K)
+    nthreads = threads if threads > 0 else oracle.default_threads()
+    # Calibrate: rows per second with all threads.
+    probe = max(nthreads, 8)
+    rows = rng.integers(0, a_rows, probe).astype(np.int32)
+    t0 = time.perf_counter()
+    oracle.gemm_nt_rows(adq, bdq, rows, threads=nthreads)
+    dt = time.perf_counter() - t0
+    n_rows = max(nthreads, int(probe * target_s / max(dt, 1e-6)))
+    n_rows = min(n_rows, M)
+    rows = rng.integers(0, a_rows, n_rows).astype(np.int32)
+    t0 = time.perf_counter()
+    oracle.gemm_nt_rows(adq, bdq, rows, threads=nthreads)
+    dt = time.perf_counter() - t0
+    return 2.0 * n_rows * N * K / dt / 1e12, n_rows, dt, nthreads
+
+
+def run_reference(args, rank, world):
+    cfg = CONFIGS[args.config]
+    M, N, K, od, desc = cfg
+    if rank != 0:
+        return 0
+    per_step = []
+    sample_rows = 0
+    cores = 0
+    for i in range(args.warmup + args.steps):
+        tf, nr, dt, cores = cpu_reference_sample(M, N, K, target_s=args.ref_step_s)
+        if i >= args.warmup:
+            per_step.append((tf, nr, dt))
+            sample_rows = nr
+    tot_flops = sum(2.0 * nr * N * K for _, nr, _ in per_step)
+    tot_t = sum(dt for _, _, dt in per_step)
+    val = tot_flops / tot_t / 1e12
+    line = {
+        "impl": "reference", "metric": "nvfp4_gemm_tflops", "value": val, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * tot_t / len(per_step), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": desc, "M": M, "N": N, "K": K},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample_rows} seeded output rows of {M} per step "
+                                   f"(x{N} cols, K={K}); naive FP32 k-ascending oracle"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------- b200 arm
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from nvfp4bench_b200 import api
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    M, N, K, od, desc = CONFIGS[args.config]
+    out_dtype = torch.bfloat16 if od == "bf16" else torch.float32
+    out_bytes = 2 if od == "bf16" else 4
+    stream = torch.cuda.current_stream()
+
+    # Operands: A replicated (same seed on every rank), B = this rank's N-slice of a
+    # world*N-wide weight (seed offset by rank).
+    x = api.fill_normal(M, K, SEED_A)
+    A = api.quantize(x, canonical=False, tcgen05=True)
+    del x
+    x = api.fill_normal(N, K, SEED_B + rank)
+    B = api.quantize(x, canonical=False, tcgen05=True)
+    del x
+    C = torch.empty((M, N), dtype=out_dtype, device=dev)
+    gargs = api.gemm_args(A.packed, A.scales_tc, B.packed, B.scales_tc, M, N, K, C,
+                          sf_layout=api.SF_TCGEN05, tile_n=args.tile_n)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    # Measured roofs for this run (tcgen05 FP4 ladder, HBM copy).
+    peak_tf = api.peak(256, torch.cuda.get_device_properties(dev).multi_processor_count, 4096, 5)
+
+    def step():
+        api.launch(gargs)
+
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    mean_ms = sum(times) / len(times)
+    min_ms, med_ms = min(times), statistics.median(times)
+    t = torch.tensor([mean_ms, min_ms, med_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    mean_ms, min_ms, med_ms = t.tolist()
+    derr = api.device_error()
+    if derr:
+        raise RuntimeError(f"device error word {derr:#x}")
+
+    flops = 2.0 * M * N * K
+    value = world * flops / (mean_ms * 1e-3) / 1e12
+    achieved = flops / (mean_ms * 1e-3) / 1e12
+
+    # Reference-style timing (src/bench.cu:90-105): per-launch events, no flush, burst=min,
+    # sustained=median of 50.
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(50)]
+    for s_, e_ in ev:
+        s_.record(stream)
+        step()
+        e_.record(stream)
+    torch.cuda.synchronize()
+    rt = sorted(s_.elapsed_time(e_) for s_, e_ in ev)
+    burst_tf, sust_tf = flops / (rt[0] * 1e-3) / 1e12, flops / (rt[len(rt) // 2] * 1e-3) / 1e12
+
+    # e2e through the C ABI with pinned host buffers.
+    hA, hAs = A.packed.cpu().pin_memory(), A.scales_tc.cpu().pin_memory()
+    hB, hBs = B.packed.cpu().pin_memory(), B.scales_tc.cpu().pin_memory()
+    hC = torch.empty((M, N), dtype=out_dtype).pin_memory()
+    dA, dAs = torch.empty_like(A.packed), torch.empty_like(A.scales_tc)
+    dB, dBs = torch.empty_like(B.packed), torch.empty_like(B.scales_tc)
+    dC = torch.empty_like(C)
+    eargs = api.gemm_args(dA, dAs, dB, dBs, M, N, K, dC, sf_layout=api.SF_TCGEN05,
+                          tile_n=args.tile_n)
+    h2d = hA.numel() + hAs.numel() + hB.numel() + hBs.numel()
+    d2h = M * N * out_bytes
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dAs.copy_(hAs, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        dBs.copy_(hBs, non_blocking=True)
+        api.launch(eargs)
+        hC.copy_(dC, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = e2e_ms.item()
+    if not torch.equal(hC.to(dev), C):
+        raise RuntimeError("e2e output differs from the device-resident output")
+
+    if rank != 0:
+        return 0
+
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tfile):
+        with open(tfile) as f:
+            traffic = json.load(f).get(args.config)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        tf, nr, dt, cores = cpu_reference_sample(M, N, K, target_s=args.cpu_seconds)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+               "sample": f"{nr} seeded output rows (x{N} cols, K={K}) in {dt:.1f} s; naive FP32 "
+                         f"k-ascending oracle (src/reference.cu restated), all host threads"}
+    line = {
+        "metric": "nvfp4_gemm_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/ue4m3->f32",
+        "data": "synthetic N(0,1), seeded, quantised on the GPU",
+        "config": {"workload": desc, "M": M, "N_per_gpu": N, "K": K, "out": od,
+                   "parallelism": f"N-sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed (256 MiB write) before every step; per-step CUDA events",
+                   "tile_n": args.tile_n or "auto", "sf_layout": "tcgen05"},
+        "burst_tflops": burst_tf, "sustained_tflops": sust_tf,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf,
+                     "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                     "peak_source": "tcgen05 kind::mxf4nvf4 ladder measured in this run "
+                                    "(M128 N256 K64, 148 CTAs)",
+                     "bf16_measured_peak": peaks.get("bf16_tflops"),
+                     "traffic": traffic,
+                     "algorithmic_bytes": algorithmic_bytes(M, N, K, out_bytes)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--tile-n", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-step-s", type=float, default=3.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        return run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

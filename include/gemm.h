@@ -1,0 +1,73 @@
+// gemm.h - launch interface of the NVFP4 GEMM backends (drop-in for the reference's
+// src/gemm.h:13-40).
+//
+// D = A * B^T with NVFP4 operands: E2M1 values packed two per byte (low nibble = even
+// index), one UE4M3 scale per 16 contiguous K elements, and one FP32 global scale per
+// tensor. FP32 accumulation.
+//
+// Layouts (the reference's own text at src/gemm.h:10-11 says B is K x N, but its CUTLASS
+// and custom backends and all of its benchmark configurations use N x K; this engine uses
+// N x K throughout):
+//   A packed [M][K/2], B packed [N][K/2].
+//   Scales, SfLayout::Canonical: [rows][K/16] row-major (src/nvfp4.h:28-38).
+//   Scales, SfLayout::Tcgen05:  512-byte atoms of 128 rows x 4 scales, atom (r/128, s/4)
+//     at ((r/128)*ceil(K/64) + s/4)*512, byte (r%32)*16 + ((r/32)%4)*4 + s%4 inside it,
+//     rows padded to 128 (see nvfp4_b200_sf_tcgen05_bytes). This is the order in which the
+//     tensor cores read scales from Tensor Memory, so no reshuffle is needed per call.
+//   Output: M x N row-major, FP32 into `c` (reference field) or, when `d` is set, the
+//     type `out_dtype` into `d`.
+//   2:4 sparse A (GemmMode::Sparse): a_packed holds the kept values [M][K/4] (two of
+//     every four, in order), a_meta the 2-bit positions of each kept value, a_scales the
+//     scales of the logical (uncompressed) K.
+#pragma once
+
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "common.h"
+
+enum class SfLayout { Canonical = 0, Tcgen05 = 1 };
+enum class OutDType { F32 = 0, BF16 = 1 };
+
+// src/gemm.h:13-23, extended with defaulted fields (a reference-style initialisation of
+// the first ten fields keeps its meaning).
+struct Nvfp4DeviceOperands {
+  const uint8_t* a_packed = nullptr;
+  const uint8_t* a_scales = nullptr;
+  float a_global = 1.0f;
+  const uint8_t* b_packed = nullptr;
+  const uint8_t* b_scales = nullptr;
+  float b_global = 1.0f;
+  float* c = nullptr;
+  int M = 0, N = 0, K = 0;
+  GemmMode mode = GemmMode::Dense;
+  // ---- engine extensions --------------------------------------------------------------
+  SfLayout sf_layout = SfLayout::Canonical;
+  OutDType out_dtype = OutDType::F32;
+  void* d = nullptr;                 // output of out_dtype; when null, `c` (FP32) is used
+  const uint8_t* a_meta = nullptr;   // 2:4 metadata (GemmMode::Sparse)
+  int cta_group = 0;                 // 0 = heuristic, 1 = one-SM tiles, 2 = SM-pair tiles
+  int tile_n = 0;                    // 0 = heuristic, else 64/128/256
+};
+
+// src/gemm.h:25-29. Each backend returns true on success; on failure it sets *err (which
+// may be null) and returns false. Launches are asynchronous on `s`; nothing synchronises.
+bool launch_gemm_stub(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
+bool launch_gemm_cutlass(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
+bool launch_gemm_custom(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
+// The B200 backend: hand-written sm_100a tcgen05 kernels (nvfp4bench_b200/csrc/gemm_b200.cu).
+bool launch_gemm_b200(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
+
+// src/gemm.h:31-40
+inline bool launch_gemm(KernelKind kind, const Nvfp4DeviceOperands& op, cudaStream_t s,
+                        std::string* err) {
+  switch (kind) {
+    case KernelKind::Stub: return launch_gemm_stub(op, s, err);
+    case KernelKind::Cutlass: return launch_gemm_cutlass(op, s, err);
+    case KernelKind::Custom: return launch_gemm_custom(op, s, err);
+    case KernelKind::B200: return launch_gemm_b200(op, s, err);
+  }
+  if (err) *err = "unknown kernel kind";
+  return false;
+}

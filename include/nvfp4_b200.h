@@ -1,0 +1,120 @@
+/* nvfp4_b200.h - C ABI of the B200 NVFP4 GEMM engine (libnvfp4_b200.so).
+ *
+ * Plain pointers and sizes only. Every entry point returns 0 on success, or a nonzero
+ * NVFP4_B200_E* code with a message copied into `err` (up to errlen bytes, may be NULL);
+ * none throws or exits, and all launches are asynchronous on `stream` (a cudaStream_t; NULL
+ * = legacy default stream) on the current device. Device buffers belong to the caller.
+ * This is the surface a ctypes / cgo / JNI binding of the reference's hot path binds;
+ * each declaration names the reference interface it replaces (paths inside the reference
+ * project).
+ */
+#ifndef NVFP4_B200_H
+#define NVFP4_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  NVFP4_B200_OK = 0,
+  NVFP4_B200_EINVAL = 1,       /* bad argument (null pointer, unsupported shape or mode) */
+  NVFP4_B200_ECUDA = 2,        /* a CUDA runtime/driver call failed */
+  NVFP4_B200_EUNSUPPORTED = 3, /* device is not sm_100 or the feature is not built */
+  NVFP4_B200_EDEVICE = 4       /* a kernel reported a bounded-wait timeout (device error word) */
+};
+
+/* GemmMode / SfLayout / OutDType values (include/gemm.h). */
+enum { NVFP4_MODE_DENSE = 0, NVFP4_MODE_SPARSE24 = 1 };
+enum { NVFP4_SF_CANONICAL = 0, NVFP4_SF_TCGEN05 = 1 };
+enum { NVFP4_OUT_F32 = 0, NVFP4_OUT_BF16 = 1 };
+
+/* Flat form of Nvfp4DeviceOperands (include/gemm.h; reference src/gemm.h:13-23). */
+typedef struct Nvfp4GemmArgs {
+  const void* a_packed; /* [M][K/2] (dense) or [M][K/4] kept values (2:4) */
+  const void* a_scales; /* per sf_layout, over the logical K */
+  float a_global;
+  const void* b_packed; /* [N][K/2] */
+  const void* b_scales;
+  float b_global;
+  void* c;              /* M x N row-major, element type out_dtype */
+  int M, N, K;
+  int mode;             /* NVFP4_MODE_* */
+  int sf_layout;        /* NVFP4_SF_* */
+  int out_dtype;        /* NVFP4_OUT_* */
+  const void* a_meta;   /* 2:4 metadata, mode == NVFP4_MODE_SPARSE24 only */
+  int cta_group;        /* 0 = heuristic, 1 or 2 */
+  int tile_n;           /* 0 = heuristic, else 64, 128 or 256 */
+} Nvfp4GemmArgs;
+
+/* Replaces launch_gemm(KernelKind::Custom, op, s, err) - src/gemm.h:31-40 and the
+ * custom backend src/gemm_custom.cu:134-159 - with the tcgen05 backend. With
+ * NVFP4_SF_CANONICAL the call reorders the scales into a per-device workspace first. */
+int nvfp4_b200_gemm(const Nvfp4GemmArgs* args, void* stream, char* err, size_t errlen);
+
+/* Replaces quantize_to_nvfp4 - src/nvfp4.h:40-42, src/nvfp4.cu:62-97 - on the GPU,
+ * byte-identical to it. src: fp32 [rows][cols] (cols % 16 == 0). Writes packed
+ * [rows][cols/2], and the scales in the canonical layout (scales, may be NULL) and/or the
+ * tcgen05 layout (scales_tcgen05, may be NULL; nvfp4_b200_sf_tcgen05_bytes(rows, cols)). */
+int nvfp4_b200_quantize(const float* src, int rows, int cols, float global_scale,
+                        void* packed, void* scales, void* scales_tcgen05, void* stream,
+                        char* err, size_t errlen);
+
+/* Replaces dequantize_nvfp4 - src/nvfp4.h:44-45, src/nvfp4.cu:99-112 - on the GPU. */
+int nvfp4_b200_dequantize(const void* packed, const void* scales, int rows, int cols,
+                          float global_scale, float* out, void* stream, char* err,
+                          size_t errlen);
+
+/* Replaces make_random_matrix - src/nvfp4.h:47-48, src/nvfp4.cu:115-129 - on the GPU,
+ * bit-identical (splitmix64 -> uniform [-1,1)). */
+int nvfp4_b200_fill_uniform(float* out, int rows, int cols, uint64_t seed, void* stream,
+                            char* err, size_t errlen);
+
+/* N(0,1) fill (no reference counterpart; the benchmark configurations ask for it):
+ * element i = Box-Muller of two splitmix64 uniforms of (seed, i). Deterministic per GPU
+ * build; not bit-identical to any CPU implementation (device logf/cosf). */
+int nvfp4_b200_fill_normal(float* out, int rows, int cols, uint64_t seed, void* stream,
+                           char* err, size_t errlen);
+
+/* Size in bytes of the tcgen05 scale layout for a [rows x K] operand. No reference
+ * counterpart (the reference's CUTLASS backend builds its own, src/gemm_cutlass.cu:151-152). */
+size_t nvfp4_b200_sf_tcgen05_bytes(int rows, int K);
+
+/* Canonical [rows][K/16] scales -> tcgen05 layout (padding written as zero). */
+int nvfp4_b200_sf_to_tcgen05(const void* scales, int rows, int K, void* out, void* stream,
+                             char* err, size_t errlen);
+
+/* Replaces measure_bandwidth_gbs - src/bench.h:24, src/bandwidth.cu:14-52 - as the HBM
+ * roof. kind 0 = copy (read+write), 1 = read-only stream, 2 = triad c=a+s*b (3 arrays).
+ * Uses caller-provided device buffers of `bytes` each (src, dst, src2 for triad; dst may
+ * be NULL for kind 1). Returns the best GB/s over `iters` timed launches in *gbs. */
+int nvfp4_b200_measure_bandwidth(int kind, const void* src, void* dst, const void* src2,
+                                 size_t bytes, int iters, double* gbs, void* stream, char* err,
+                                 size_t errlen);
+
+/* Replaces run_peak_ladder - src/peak.h:8, src/peak.cu:119-156 - with a memory-free
+ * tcgen05 rung: `ctas` CTAs each issue `iters` back-to-back block-scaled MMAs of shape
+ * M=128 x n x K=64 (kind::mxf4nvf4, sparse = 0) into TMEM. *tflops = 2*128*n*64*ctas*iters
+ * / best time over `reps` launches. */
+int nvfp4_b200_peak(int n, int ctas, int iters, int reps, double* tflops, void* stream,
+                    char* err, size_t errlen);
+
+/* Reads (and when clear != 0 resets) the device error word the kernels write when a
+ * bounded wait times out (bit meanings in nvfp4bench_b200/csrc/ptx.cuh). Synchronises
+ * the current device. Returns 0 on success with the word in *word. */
+int nvfp4_b200_device_error(int clear, uint32_t* word, char* err, size_t errlen);
+
+/* Bounded-wait self test: one CTA waits on an mbarrier that nothing completes, with a
+ * limit of `limit_ns`; the kernel records NVFP4 error bit kErrTest and returns. The
+ * context stays usable. Returns the device error word in *word. */
+int nvfp4_b200_wait_selftest(uint64_t limit_ns, uint32_t* word, char* err, size_t errlen);
+
+/* Library version string. */
+const char* nvfp4_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

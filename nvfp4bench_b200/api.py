@@ -1,0 +1,223 @@
+"""ctypes binding of the engine's C ABI (include/nvfp4_b200.h) plus torch-tensor helpers.
+
+This is the binding a Python user of the reference's hot path would write against the
+C ABI; torch supplies device memory and streams only. The library is loaded from the
+package's lib/ directory (built in-tree by ``python -m nvfp4bench_b200.build``); when it is
+missing every call raises - there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import build as _build
+
+LIB_PATH = _build.LIB
+
+MODE_DENSE, MODE_SPARSE24 = 0, 1
+SF_CANONICAL, SF_TCGEN05 = 0, 1
+OUT_F32, OUT_BF16 = 0, 1
+
+# Every symbol include/nvfp4_b200.h declares (checked by the CPU tests).
+EXPORTED = [
+    "nvfp4_b200_gemm", "nvfp4_b200_quantize", "nvfp4_b200_dequantize",
+    "nvfp4_b200_fill_uniform", "nvfp4_b200_fill_normal", "nvfp4_b200_sf_tcgen05_bytes",
+    "nvfp4_b200_sf_to_tcgen05", "nvfp4_b200_measure_bandwidth", "nvfp4_b200_peak",
+    "nvfp4_b200_device_error", "nvfp4_b200_wait_selftest", "nvfp4_b200_version",
+]
+
+
+class Nvfp4Error(RuntimeError):
+    """A nonzero return code of the C ABI, with its message."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[nvfp4_b200 error {code}] {msg}")
+        self.code = code
+
+
+class GemmArgs(C.Structure):
+    """Nvfp4GemmArgs (include/nvfp4_b200.h)."""
+
+    _fields_ = [
+        ("a_packed", C.c_void_p), ("a_scales", C.c_void_p), ("a_global", C.c_float),
+        ("b_packed", C.c_void_p), ("b_scales", C.c_void_p), ("b_global", C.c_float),
+        ("c", C.c_void_p), ("M", C.c_int), ("N", C.c_int), ("K", C.c_int),
+        ("mode", C.c_int), ("sf_layout", C.c_int), ("out_dtype", C.c_int),
+        ("a_meta", C.c_void_p), ("cta_group", C.c_int), ("tile_n", C.c_int),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    """Load libnvfp4_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing; build it with `python -m nvfp4bench_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        vp, sz, ip = C.c_void_p, C.c_size_t, C.c_int
+        errs = [C.c_char_p, sz]
+        L.nvfp4_b200_gemm.argtypes = [C.POINTER(GemmArgs), vp, *errs]
+        L.nvfp4_b200_quantize.argtypes = [vp, ip, ip, C.c_float, vp, vp, vp, vp, *errs]
+        L.nvfp4_b200_dequantize.argtypes = [vp, vp, ip, ip, C.c_float, vp, vp, *errs]
+        L.nvfp4_b200_fill_uniform.argtypes = [vp, ip, ip, C.c_uint64, vp, *errs]
+        L.nvfp4_b200_fill_normal.argtypes = [vp, ip, ip, C.c_uint64, vp, *errs]
+        L.nvfp4_b200_sf_tcgen05_bytes.argtypes = [ip, ip]
+        L.nvfp4_b200_sf_tcgen05_bytes.restype = sz
+        L.nvfp4_b200_sf_to_tcgen05.argtypes = [vp, ip, ip, vp, vp, *errs]
+        L.nvfp4_b200_measure_bandwidth.argtypes = [ip, vp, vp, vp, sz, ip,
+                                                   C.POINTER(C.c_double), vp, *errs]
+        L.nvfp4_b200_peak.argtypes = [ip, ip, ip, ip, C.POINTER(C.c_double), vp, *errs]
+        L.nvfp4_b200_device_error.argtypes = [ip, C.POINTER(C.c_uint32), *errs]
+        L.nvfp4_b200_wait_selftest.argtypes = [C.c_uint64, C.POINTER(C.c_uint32), *errs]
+        L.nvfp4_b200_version.restype = C.c_char_p
+        for name in EXPORTED:
+            if name not in ("nvfp4_b200_sf_tcgen05_bytes", "nvfp4_b200_version"):
+                getattr(L, name).restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def _call(fn, *args):
+    buf = C.create_string_buffer(512)
+    rc = fn(*args, buf, len(buf))
+    if rc != 0:
+        raise Nvfp4Error(rc, buf.value.decode(errors="replace"))
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+# ---- entry points -------------------------------------------------------------------------
+def gemm(a_packed, a_scales, b_packed, b_scales, M: int, N: int, K: int, out: torch.Tensor,
+         a_global: float = 1.0, b_global: float = 1.0, sf_layout: int = SF_TCGEN05,
+         mode: int = MODE_DENSE, a_meta=None, cta_group: int = 0, tile_n: int = 0,
+         stream=None) -> torch.Tensor:
+    """D = (a_global*b_global) * A @ B^T into `out` (float32 or bfloat16, [M, N])."""
+    if out.dtype == torch.float32:
+        od = OUT_F32
+    elif out.dtype == torch.bfloat16:
+        od = OUT_BF16
+    else:
+        raise ValueError("out must be float32 or bfloat16")
+    args = GemmArgs(_ptr(a_packed), _ptr(a_scales), a_global, _ptr(b_packed), _ptr(b_scales),
+                    b_global, _ptr(out), M, N, K, mode, sf_layout, od, _ptr(a_meta), cta_group,
+                    tile_n)
+    _call(lib().nvfp4_b200_gemm, C.byref(args), _stream(stream))
+    return out
+
+
+def gemm_args(a_packed, a_scales, b_packed, b_scales, M, N, K, out, **kw) -> GemmArgs:
+    """Prebuilt argument block for repeated launches (see launch())."""
+    od = OUT_BF16 if out.dtype == torch.bfloat16 else OUT_F32
+    return GemmArgs(_ptr(a_packed), _ptr(a_scales), kw.get("a_global", 1.0), _ptr(b_packed),
+                    _ptr(b_scales), kw.get("b_global", 1.0), _ptr(out), M, N, K,
+                    kw.get("mode", MODE_DENSE), kw.get("sf_layout", SF_TCGEN05), od,
+                    _ptr(kw.get("a_meta")), kw.get("cta_group", 0), kw.get("tile_n", 0))
+
+
+def launch(args: GemmArgs, stream=None) -> None:
+    _call(lib().nvfp4_b200_gemm, C.byref(args), _stream(stream))
+
+
+def sf_tcgen05_bytes(rows: int, K: int) -> int:
+    return int(lib().nvfp4_b200_sf_tcgen05_bytes(rows, K))
+
+
+@dataclass
+class Nvfp4Tensor:
+    """Device NVFP4 tensor (the reference's Nvfp4Tensor, src/nvfp4.h:28-38, on the GPU)."""
+
+    rows: int
+    cols: int
+    global_scale: float
+    packed: torch.Tensor             # uint8 [rows, cols/2]
+    scales: Optional[torch.Tensor]   # uint8 [rows, cols/16] canonical
+    scales_tc: Optional[torch.Tensor]  # uint8 [sf_tcgen05_bytes] tcgen05 layout
+
+
+def quantize(x: torch.Tensor, global_scale: float = 1.0, canonical: bool = True,
+             tcgen05: bool = True, stream=None) -> Nvfp4Tensor:
+    """GPU quantize_to_nvfp4 (byte-identical to src/nvfp4.cu:62-97)."""
+    assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous() and x.dim() == 2
+    rows, cols = x.shape
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=x.device)
+    sc = torch.empty((rows, cols // 16), dtype=torch.uint8, device=x.device) if canonical else None
+    tc = torch.empty(sf_tcgen05_bytes(rows, cols), dtype=torch.uint8, device=x.device) \
+        if tcgen05 else None
+    _call(lib().nvfp4_b200_quantize, x.data_ptr(), rows, cols, global_scale, packed.data_ptr(),
+          _ptr(sc), _ptr(tc), _stream(stream))
+    return Nvfp4Tensor(rows, cols, global_scale, packed, sc, tc)
+
+
+def dequantize(t: Nvfp4Tensor, stream=None) -> torch.Tensor:
+    out = torch.empty((t.rows, t.cols), dtype=torch.float32, device=t.packed.device)
+    _call(lib().nvfp4_b200_dequantize, t.packed.data_ptr(), t.scales.data_ptr(), t.rows, t.cols,
+          t.global_scale, out.data_ptr(), _stream(stream))
+    return out
+
+
+def fill_uniform(rows: int, cols: int, seed: int, device="cuda", stream=None) -> torch.Tensor:
+    out = torch.empty((rows, cols), dtype=torch.float32, device=device)
+    _call(lib().nvfp4_b200_fill_uniform, out.data_ptr(), rows, cols, seed, _stream(stream))
+    return out
+
+
+def fill_normal(rows: int, cols: int, seed: int, device="cuda", stream=None) -> torch.Tensor:
+    out = torch.empty((rows, cols), dtype=torch.float32, device=device)
+    _call(lib().nvfp4_b200_fill_normal, out.data_ptr(), rows, cols, seed, _stream(stream))
+    return out
+
+
+def sf_to_tcgen05(scales: torch.Tensor, rows: int, K: int, stream=None) -> torch.Tensor:
+    out = torch.empty(sf_tcgen05_bytes(rows, K), dtype=torch.uint8, device=scales.device)
+    _call(lib().nvfp4_b200_sf_to_tcgen05, scales.data_ptr(), rows, K, out.data_ptr(),
+          _stream(stream))
+    return out
+
+
+def measure_bandwidth(kind: int, src: torch.Tensor, dst: Optional[torch.Tensor],
+                      src2: Optional[torch.Tensor], nbytes: int, iters: int = 10,
+                      stream=None) -> float:
+    g = C.c_double(0.0)
+    _call(lib().nvfp4_b200_measure_bandwidth, kind, src.data_ptr(), _ptr(dst), _ptr(src2), nbytes,
+          iters, C.byref(g), _stream(stream))
+    return g.value
+
+
+def peak(n: int = 256, ctas: int = 148, iters: int = 4096, reps: int = 5, stream=None) -> float:
+    t = C.c_double(0.0)
+    _call(lib().nvfp4_b200_peak, n, ctas, iters, reps, C.byref(t), _stream(stream))
+    return t.value
+
+
+def device_error(clear: bool = True) -> int:
+    w = C.c_uint32(0)
+    _call(lib().nvfp4_b200_device_error, 1 if clear else 0, C.byref(w))
+    return int(w.value)
+
+
+def wait_selftest(limit_ns: int = 20_000_000) -> int:
+    w = C.c_uint32(0)
+    _call(lib().nvfp4_b200_wait_selftest, limit_ns, C.byref(w))
+    return int(w.value)
+
+
+def version() -> str:
+    return lib().nvfp4_b200_version().decode()

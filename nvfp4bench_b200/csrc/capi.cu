@@ -1,0 +1,184 @@
+// capi.cu - the C ABI (include/nvfp4_b200.h) over the engine's C++ entry points, and the
+// reference's GB10-only backend slots, which this engine does not build.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <string>
+
+#include "gemm.h"
+#include "internal.h"
+#include "nvfp4_b200.h"
+
+namespace {
+
+int fail(int code, const std::string& msg, char* err, size_t errlen) {
+  if (err && errlen) {
+    size_t n = msg.size() < errlen - 1 ? msg.size() : errlen - 1;
+    std::memcpy(err, msg.data(), n);
+    err[n] = '\0';
+  }
+  return code;
+}
+
+int ok(char* err, size_t errlen) {
+  if (err && errlen) err[0] = '\0';
+  return NVFP4_B200_OK;
+}
+
+// Argument errors are EINVAL; anything that mentions CUDA is ECUDA.
+int classify(const std::string& msg) {
+  if (msg.find("sm_100") != std::string::npos) return NVFP4_B200_EUNSUPPORTED;
+  if (msg.find("not built") != std::string::npos || msg.find("not supported") != std::string::npos)
+    return NVFP4_B200_EUNSUPPORTED;
+  if (msg.find("cuda") != std::string::npos || msg.find("CUDA") != std::string::npos ||
+      msg.find("launch") != std::string::npos || msg.find("failed") != std::string::npos)
+    return NVFP4_B200_ECUDA;
+  return NVFP4_B200_EINVAL;
+}
+
+}  // namespace
+
+// The reference's GB10 backends (src/gemm_stub.cu, src/gemm_cutlass.cu, src/gemm_custom.cu)
+// use sm_120a warp-level MMAs that do not exist on sm_100a; like the reference's own
+// "not built" stubs (src/gemm_custom.cu:18-23) they report that and return false.
+bool launch_gemm_stub(const Nvfp4DeviceOperands&, cudaStream_t, std::string* err) {
+  if (err) *err = "stub backend not built (GB10 reference backend; use --kernel b200)";
+  return false;
+}
+bool launch_gemm_cutlass(const Nvfp4DeviceOperands&, cudaStream_t, std::string* err) {
+  if (err) *err = "cutlass backend not built (GB10 reference backend; use --kernel b200)";
+  return false;
+}
+bool launch_gemm_custom(const Nvfp4DeviceOperands&, cudaStream_t, std::string* err) {
+  if (err) *err = "custom backend not built (GB10 reference backend; use --kernel b200)";
+  return false;
+}
+
+extern "C" {
+
+int nvfp4_b200_gemm(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errlen) {
+  if (!a) return fail(NVFP4_B200_EINVAL, "null args", err, errlen);
+  Nvfp4DeviceOperands op;
+  op.a_packed = static_cast<const uint8_t*>(a->a_packed);
+  op.a_scales = static_cast<const uint8_t*>(a->a_scales);
+  op.a_global = a->a_global;
+  op.b_packed = static_cast<const uint8_t*>(a->b_packed);
+  op.b_scales = static_cast<const uint8_t*>(a->b_scales);
+  op.b_global = a->b_global;
+  op.M = a->M;
+  op.N = a->N;
+  op.K = a->K;
+  if (a->mode != NVFP4_MODE_DENSE && a->mode != NVFP4_MODE_SPARSE24)
+    return fail(NVFP4_B200_EINVAL, "unknown mode", err, errlen);
+  if (a->sf_layout != NVFP4_SF_CANONICAL && a->sf_layout != NVFP4_SF_TCGEN05)
+    return fail(NVFP4_B200_EINVAL, "unknown sf_layout", err, errlen);
+  if (a->out_dtype != NVFP4_OUT_F32 && a->out_dtype != NVFP4_OUT_BF16)
+    return fail(NVFP4_B200_EINVAL, "unknown out_dtype", err, errlen);
+  op.mode = a->mode == NVFP4_MODE_SPARSE24 ? GemmMode::Sparse : GemmMode::Dense;
+  op.sf_layout = a->sf_layout == NVFP4_SF_TCGEN05 ? SfLayout::Tcgen05 : SfLayout::Canonical;
+  op.out_dtype = a->out_dtype == NVFP4_OUT_BF16 ? OutDType::BF16 : OutDType::F32;
+  op.d = a->c;
+  op.a_meta = static_cast<const uint8_t*>(a->a_meta);
+  op.cta_group = a->cta_group;
+  op.tile_n = a->tile_n;
+  std::string e;
+  if (!launch_gemm_b200(op, static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_quantize(const float* src, int rows, int cols, float global_scale, void* packed,
+                        void* scales, void* scales_tc, void* stream, char* err, size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::quantize(src, rows, cols, global_scale, static_cast<uint8_t*>(packed),
+                           static_cast<uint8_t*>(scales), static_cast<uint8_t*>(scales_tc),
+                           static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_dequantize(const void* packed, const void* scales, int rows, int cols,
+                          float global_scale, float* out, void* stream, char* err, size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::dequantize(static_cast<const uint8_t*>(packed), static_cast<const uint8_t*>(scales),
+                             rows, cols, global_scale, out, static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_fill_uniform(float* out, int rows, int cols, uint64_t seed, void* stream, char* err,
+                            size_t errlen) {
+  if (rows < 0 || cols < 0) return fail(NVFP4_B200_EINVAL, "negative size", err, errlen);
+  std::string e;
+  if (!nvfp4b200::fill_uniform(out, static_cast<size_t>(rows) * cols, seed,
+                               static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_fill_normal(float* out, int rows, int cols, uint64_t seed, void* stream, char* err,
+                           size_t errlen) {
+  if (rows < 0 || cols < 0) return fail(NVFP4_B200_EINVAL, "negative size", err, errlen);
+  std::string e;
+  if (!nvfp4b200::fill_normal(out, static_cast<size_t>(rows) * cols, seed,
+                              static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+size_t nvfp4_b200_sf_tcgen05_bytes(int rows, int K) {
+  if (rows <= 0 || K <= 0) return 0;
+  return nvfp4b200::sf_tcgen05_bytes(rows, K);
+}
+
+int nvfp4_b200_sf_to_tcgen05(const void* scales, int rows, int K, void* out, void* stream,
+                             char* err, size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::sf_to_tcgen05(static_cast<const uint8_t*>(scales), rows, K,
+                                static_cast<uint8_t*>(out), static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_measure_bandwidth(int kind, const void* src, void* dst, const void* src2,
+                                 size_t bytes, int iters, double* gbs, void* stream, char* err,
+                                 size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::measure_bandwidth(kind, src, dst, src2, bytes, iters, gbs,
+                                    static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_peak(int n, int ctas, int iters, int reps, double* tflops, void* stream, char* err,
+                    size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::peak_ladder(n, ctas, iters, reps, tflops, static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_device_error(int clear, uint32_t* word, char* err, size_t errlen) {
+  std::string e;
+  uint32_t* ew = nvfp4b200::device_error_word(&e);
+  if (!ew) return fail(NVFP4_B200_ECUDA, e, err, errlen);
+  if (cudaDeviceSynchronize() != cudaSuccess)
+    return fail(NVFP4_B200_ECUDA, "cudaDeviceSynchronize failed", err, errlen);
+  uint32_t w = 0;
+  if (cudaMemcpy(&w, ew, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(NVFP4_B200_ECUDA, "reading the device error word failed", err, errlen);
+  if (clear && cudaMemset(ew, 0, sizeof(uint32_t)) != cudaSuccess)
+    return fail(NVFP4_B200_ECUDA, "clearing the device error word failed", err, errlen);
+  if (word) *word = w;
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_wait_selftest(uint64_t limit_ns, uint32_t* word, char* err, size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::wait_selftest(limit_ns, &e)) return fail(classify(e), e, err, errlen);
+  return nvfp4_b200_device_error(1, word, err, errlen);
+}
+
+const char* nvfp4_b200_version(void) { return "nvfp4-b200 0.1.0 (sm_100a tcgen05)"; }
+
+}  // extern "C"

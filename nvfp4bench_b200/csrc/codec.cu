@@ -1,0 +1,280 @@
+// codec.cu - NVFP4 codecs on the GPU, byte-identical to the reference's host codecs.
+//
+// Restated from src/nvfp4.cu (reference project):
+//   e2m1_quantize  :18-29  nearest of {0,.5,1,1.5,2,3,4,6}, ties to the smaller magnitude
+//   e4m3_decode    :34-45  UE4M3, bias 7, subnormals; code 0x7F decodes to 480
+//   e4m3_encode    :47-59  nearest code in 0..127, ties to the lower code, x clamped to 448
+//   quantize       :62-97  per-16 amax -> scale (amax/6)/g -> code -> x / (dec(code)*g)
+//   dequantize     :99-112
+//   make_random    :115-129 splitmix64 -> uniform [-1, 1)
+// Every float operation is the same IEEE single operation as in the host code (explicit
+// __fdiv_rn / __fmul_rn, no contraction), so bytes match exactly. The linear 128-way scale
+// search becomes a binary search for the first code whose value is >= x followed by the
+// reference's own error comparison between that code and the one below it: decoded values
+// strictly increase with the code, so the nearest code is one of those two, and an exact
+// tie keeps the lower code as the linear search does.
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "internal.h"
+
+namespace nvfp4b200 {
+namespace {
+
+constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;
+
+__device__ __forceinline__ uint64_t splitmix_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// src/nvfp4.cu:34-45 for positive codes, built from the bit pattern (exact).
+__device__ __forceinline__ float e4m3_decode_pos(int c) {
+  const int e = (c >> 3) & 0xF, m = c & 7;
+  if (e == 0) return __fmul_rn(static_cast<float>(m), 0.001953125f);  // m/8 * 2^-6
+  return __int_as_float(((e + 120) << 23) | (m << 20));                 // (1+m/8) * 2^(e-7)
+}
+__device__ __forceinline__ float e4m3_decode_dev(uint8_t code) {
+  const float v = e4m3_decode_pos(code & 0x7F);
+  return (code & 0x80) ? -v : v;
+}
+
+__device__ __forceinline__ uint8_t e4m3_encode_dev(float x) {
+  if (!(x > 0.0f)) return 0;  // x <= 0 -> 0; NaN -> 0 (no error ever compares smaller)
+  if (448.0f < x) x = 448.0f;
+  int lo = 1, hi = 126;       // dec(0) = 0 < x and dec(126) = 448 >= x
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (e4m3_decode_pos(mid) >= x) hi = mid; else lo = mid + 1;
+  }
+  const float eh = fabsf(__fsub_rn(e4m3_decode_pos(hi), x));
+  const float el = fabsf(__fsub_rn(e4m3_decode_pos(hi - 1), x));
+  return static_cast<uint8_t>(eh < el ? hi : hi - 1);
+}
+
+// src/nvfp4.cu:18-29, verbatim in structure.
+__device__ __forceinline__ uint8_t e2m1_quantize_dev(float x) {
+  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  const uint8_t sign = (x < 0.0f) ? 0x8 : 0x0;
+  const float a = fabsf(x);
+  int best = 0;
+  float best_err = fabsf(__fsub_rn(a, mag[0]));
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    const float e = fabsf(__fsub_rn(a, mag[i]));
+    if (e < best_err) { best_err = e; best = i; }
+  }
+  return static_cast<uint8_t>(sign | best);
+}
+
+__device__ __forceinline__ float e2m1_decode_dev(uint8_t code) {
+  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  const float m = mag[code & 7];
+  return (code & 8) ? -m : m;
+}
+
+__global__ void fill_uniform_kernel(float* __restrict__ out, size_t n, uint64_t x0) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n;
+       i += size_t(gridDim.x) * blockDim.x) {
+    const uint64_t z = splitmix_mix(x0 + static_cast<uint64_t>(i + 1) * kGolden);
+    out[i] = __fsub_rn(__fmul_rn(__fdiv_rn(static_cast<float>(z >> 40), 16777216.0f), 2.0f), 1.0f);
+  }
+}
+
+__global__ void fill_normal_kernel(float* __restrict__ out, size_t n, uint64_t x0) {
+  const size_t pairs = (n + 1) / 2;
+  for (size_t p = blockIdx.x * size_t(blockDim.x) + threadIdx.x; p < pairs;
+       p += size_t(gridDim.x) * blockDim.x) {
+    const uint64_t z1 = splitmix_mix(x0 + static_cast<uint64_t>(2 * p + 1) * kGolden);
+    const uint64_t z2 = splitmix_mix(x0 + static_cast<uint64_t>(2 * p + 2) * kGolden);
+    const float u1 = (static_cast<float>(z1 >> 40) + 1.0f) * (1.0f / 16777216.0f);  // (0, 1]
+    const float u2 = static_cast<float>(z2 >> 40) * (1.0f / 16777216.0f);           // [0, 1)
+    const float r = sqrtf(-2.0f * logf(u1));
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    out[2 * p] = r * cs;
+    if (2 * p + 1 < n) out[2 * p + 1] = r * sn;
+  }
+}
+
+// One thread per 16-element block (src/nvfp4.cu:66-95).
+__global__ void quantize_kernel(const float* __restrict__ src, int rows, int cols, float g,
+                                uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
+                                uint8_t* __restrict__ scales_tc, int ka) {
+  const int nb = cols / 16;
+  const size_t nblocks = static_cast<size_t>(rows) * nb;
+  for (size_t blk = blockIdx.x * size_t(blockDim.x) + threadIdx.x; blk < nblocks;
+       blk += size_t(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(blk / nb), b = static_cast<int>(blk % nb);
+    const float4* x4 = reinterpret_cast<const float4*>(src + static_cast<size_t>(r) * cols + b * 16);
+    float x[16];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const float4 t = x4[v];
+      x[4 * v] = t.x; x[4 * v + 1] = t.y; x[4 * v + 2] = t.z; x[4 * v + 3] = t.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float a = fabsf(x[j]);
+      if (amax < a) amax = a;  // std::max(amax, a): NaN never replaces amax
+    }
+    const float scale = (amax > 0.0f) ? __fdiv_rn(__fdiv_rn(amax, 6.0f), g) : 1.0f;
+    const uint8_t sc = e4m3_encode_dev(scale);
+    float dec = __fmul_rn(e4m3_decode_dev(sc), g);
+    if (dec <= 0.0f) dec = 1.0f;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) lo |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[j], dec))) << (4 * j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hi |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[8 + j], dec))) << (4 * j);
+    *reinterpret_cast<uint2*>(packed + (static_cast<size_t>(r) * cols + b * 16) / 2) = make_uint2(lo, hi);
+    if (scales) scales[blk] = sc;
+    if (scales_tc) {
+      const size_t atom = static_cast<size_t>(r / 128) * ka + b / 4;
+      scales_tc[atom * 512 + (r % 32) * 16 + ((r / 32) % 4) * 4 + (b % 4)] = sc;
+    }
+  }
+}
+
+// src/nvfp4.cu:99-112, one thread per 16-element block.
+__global__ void dequantize_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ scales,
+                                  int rows, int cols, float g, float* __restrict__ out) {
+  const int nb = cols / 16;
+  const size_t nblocks = static_cast<size_t>(rows) * nb;
+  for (size_t blk = blockIdx.x * size_t(blockDim.x) + threadIdx.x; blk < nblocks;
+       blk += size_t(gridDim.x) * blockDim.x) {
+    const float s = __fmul_rn(e4m3_decode_dev(scales[blk]), g);
+    const size_t e0 = (blk / nb) * static_cast<size_t>(cols) + (blk % nb) * 16;
+    const uint2 w = *reinterpret_cast<const uint2*>(packed + e0 / 2);
+    float4* o = reinterpret_cast<float4*>(out + e0);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const uint32_t word = v < 2 ? w.x : w.y;
+      const int sh = (v & 1) * 16;
+      o[v] = make_float4(__fmul_rn(e2m1_decode_dev((word >> sh) & 0xF), s),
+                         __fmul_rn(e2m1_decode_dev((word >> (sh + 4)) & 0xF), s),
+                         __fmul_rn(e2m1_decode_dev((word >> (sh + 8)) & 0xF), s),
+                         __fmul_rn(e2m1_decode_dev((word >> (sh + 12)) & 0xF), s));
+    }
+  }
+}
+
+// Canonical [rows][K/16] -> tcgen05 atoms; one thread per output 32-bit word, zero padding.
+__global__ void sf_to_tcgen05_kernel(const uint8_t* __restrict__ scales, int rows, int ns, int ka,
+                                     size_t words, uint32_t* __restrict__ out) {
+  for (size_t w = blockIdx.x * size_t(blockDim.x) + threadIdx.x; w < words;
+       w += size_t(gridDim.x) * blockDim.x) {
+    const size_t atom = w >> 7;
+    const int wi = static_cast<int>(w & 127);
+    const int rb = static_cast<int>(atom / ka), kb = static_cast<int>(atom % ka);
+    const int row = rb * 128 + (wi & 3) * 32 + (wi >> 2);
+    uint32_t v = 0;
+    if (row < rows) {
+      const uint8_t* src = scales + static_cast<size_t>(row) * ns;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int s = kb * 4 + i;
+        if (s < ns) v |= static_cast<uint32_t>(src[s]) << (8 * i);
+      }
+    }
+    out[w] = v;
+  }
+}
+
+int grid_for(size_t work, int block) {
+  size_t g = (work + block - 1) / block;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+bool check_launch(const char* what, std::string* err) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(err, std::string(what) + ": " + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+bool fill_uniform(float* out, size_t n, uint64_t seed, cudaStream_t s, std::string* err) {
+  if (!out) { set_err(err, "null output"); return false; }
+  if (n == 0) return true;
+  const uint64_t x0 = seed ? seed : kGolden;  // src/nvfp4.cu:118
+  fill_uniform_kernel<<<grid_for(n, 256), 256, 0, s>>>(out, n, x0);
+  return check_launch("fill_uniform", err);
+}
+
+bool fill_normal(float* out, size_t n, uint64_t seed, cudaStream_t s, std::string* err) {
+  if (!out) { set_err(err, "null output"); return false; }
+  if (n == 0) return true;
+  const uint64_t x0 = seed ? seed : kGolden;
+  fill_normal_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(out, n, x0);
+  return check_launch("fill_normal", err);
+}
+
+bool quantize(const float* src, int rows, int cols, float global_scale, uint8_t* packed,
+              uint8_t* scales, uint8_t* scales_tc, cudaStream_t s, std::string* err) {
+  if (!src || !packed) { set_err(err, "null pointer"); return false; }
+  if (rows < 0 || cols < 0 || cols % 16 != 0) {
+    set_err(err, "quantize needs rows >= 0 and cols a multiple of 16");
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(packed) & 7)) {
+    set_err(err, "quantize needs a 16-byte aligned source and an 8-byte aligned packed output");
+    return false;
+  }
+  const size_t nblocks = static_cast<size_t>(rows) * (cols / 16);
+  if (nblocks == 0) return true;
+  if (scales_tc) {
+    if (cudaMemsetAsync(scales_tc, 0, sf_tcgen05_bytes(rows, cols), s) != cudaSuccess) {
+      set_err(err, "cudaMemsetAsync of the tcgen05 scale buffer failed");
+      return false;
+    }
+  }
+  quantize_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(src, rows, cols, global_scale, packed,
+                                                        scales, scales_tc, (cols + 63) / 64);
+  return check_launch("quantize", err);
+}
+
+bool dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                float global_scale, float* out, cudaStream_t s, std::string* err) {
+  if (!packed || !scales || !out) { set_err(err, "null pointer"); return false; }
+  if (rows < 0 || cols < 0 || cols % 16 != 0) {
+    set_err(err, "dequantize needs cols a multiple of 16");
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(packed) & 7)) {
+    set_err(err, "dequantize needs a 16-byte aligned output and an 8-byte aligned packed input");
+    return false;
+  }
+  const size_t nblocks = static_cast<size_t>(rows) * (cols / 16);
+  if (nblocks == 0) return true;
+  dequantize_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(packed, scales, rows, cols,
+                                                          global_scale, out);
+  return check_launch("dequantize", err);
+}
+
+bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStream_t s,
+                   std::string* err) {
+  if (!scales || !out) { set_err(err, "null pointer"); return false; }
+  if (rows <= 0 || K <= 0 || K % 16 != 0) {
+    set_err(err, "sf_to_tcgen05 needs rows > 0 and K a positive multiple of 16");
+    return false;
+  }
+  if (reinterpret_cast<uintptr_t>(out) & 3) {
+    set_err(err, "tcgen05 scale output must be 4-byte aligned");
+    return false;
+  }
+  const size_t words = sf_tcgen05_bytes(rows, K) / 4;
+  sf_to_tcgen05_kernel<<<grid_for(words, 256), 256, 0, s>>>(scales, rows, K / 16, (K + 63) / 64,
+                                                           words, reinterpret_cast<uint32_t*>(out));
+  return check_launch("sf_to_tcgen05", err);
+}
+
+}  // namespace nvfp4b200

@@ -1,0 +1,614 @@
+// gemm_b200.cu - the B200 backend: NVFP4 block-scaled GEMM on 5th-generation tensor cores.
+//
+// D[M x N] = alpha * A[M x K] * B[N x K]^T with E2M1 operands and UE4M3 scales per 16
+// K-elements, FP32 accumulation in Tensor Memory, alpha = a_global * b_global applied in the
+// epilogue. Drop-in for the reference's backend slot: launch_gemm_b200 has the signature of
+// launch_gemm_custom (src/gemm.h:27-29) and honours its ownership and error rules
+// (src/gemm.h:25-26: return false + message, never throw, never exit, async on the stream).
+//
+// Kernel design (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: per K-stage, two tiled TMA loads (A 128 x 256 FP4, B BN x 256
+//               FP4, both 128-byte-swizzled K-major) and 1-D bulk copies of the scale atoms,
+//               all completing on one mbarrier ("full"). No multicast.
+//   warp 1      MMA issuer (one lane): tcgen05.cp of the stage's scale atoms into TMEM, then
+//               four tcgen05.mma kind::mxf4nvf4 block_scale (M=128, N=BN, K=64 each);
+//               tcgen05.commit frees the smem stage ("empty") and, per tile, publishes the
+//               accumulator ("acc_full").
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, scale by alpha, convert to
+//               FP32/BF16, store. Warp w reads TMEM lane quadrant w % 4.
+// Two accumulator buffers let the epilogue of tile i overlap the MMAs of tile i+1. With
+// BN = 256 the two 256-column buffers and the 64 scale columns do not fit the 512 TMEM
+// columns side by side, so buffer 1 starts at column 192: the 64 shared columns are drained
+// first and released early ("acc_early"), the rest of the buffer afterwards.
+//
+// Every mbarrier wait is bounded (ptx.cuh); a timeout sets the device error word, all roles
+// leave their loops, in-flight copies and MMAs are drained with bounded waits, TMEM is freed
+// and the kernel returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gemm.h"
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace nvfp4b200 {
+
+__device__ uint32_t g_device_error = 0;
+
+namespace {
+
+constexpr int kBM = 128;          // rows of A per tile (= TMEM lanes)
+constexpr int kBKBytes = 128;     // one K-stage = 256 FP4 = 128 bytes per row (one swizzle atom)
+constexpr int kKBlocksPerStage = 4;  // MMA K = 64 -> 4 MMAs per stage
+constexpr int kNumThreads = 192;
+constexpr int kEpiWarp0 = 2;
+constexpr int kTmemCols = 512;
+constexpr int kSfCol = 448;       // scale factors live in TMEM columns [448, 512)
+
+template <int BN>
+struct Cfg {
+  static constexpr int kABytes = kBM * kBKBytes;                 // 16 KB
+  static constexpr int kBBytes = BN * kBKBytes;                  // 16 / 32 KB
+  static constexpr int kSfaBytes = kKBlocksPerStage * 512;       // 2 KB
+  static constexpr int kSfbBytes = (BN + 127) / 128 * kKBlocksPerStage * 512;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+  // TMEM: accumulator buffers and which 32-column chunks are shared between them.
+  static constexpr int kAccBase1 = (BN == 256) ? 192 : BN;
+  static constexpr int kChunks = BN / 32;
+  static constexpr bool kOverlap = (BN == 256);
+  static constexpr int kOverlapChunks = 2;  // columns [192, 256)
+  static constexpr int kSfbCols = (BN + 127) / 128 * 4;  // per K-block
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kAccBase1 + BN <= kSfCol, "TMEM budget");
+};
+
+struct GemmParams {
+  const uint8_t* sfa;   // tcgen05 scale layout
+  const uint8_t* sfb;
+  void* out;
+  int M, N, K;
+  int ldc;
+  float alpha;
+  int out_bf16;
+  int tiles_m, tiles_n, num_tiles;
+  int group_m;
+  int ka;               // scale atoms along K = ceil(K/64)
+  int num_kt;           // K-stages = ceil(K/256)
+  int sfb_rowblocks;    // ceil(N/128)
+  uint32_t* err_word;
+};
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& tm, int& tn) {
+  const int per_group = p.group_m * p.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * p.group_m;
+  int gsize = p.tiles_m - first_m;
+  if (gsize > p.group_m) gsize = p.group_m;
+  const int local = t - g * per_group;
+  tm = first_m + local % gsize;
+  tn = local / gsize;
+}
+
+// Bounded wait that ignores the abort flag (used to drain in-flight work after an abort).
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, uint32_t* err) {
+  volatile int never = 0;
+  return mbar_wait(bar, parity, &never, err, kErrWaitDrain);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_mxf4nvf4_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                         const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + C::kStages * C::kABytes;
+  uint8_t* sSFA = sB + C::kStages * C::kBBytes;
+  uint8_t* sSFB = sSFA + C::kStages * C::kSfaBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + C::kStages * C::kSfbBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::kStages;
+  uint64_t* acc_full = bars + 2 * C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* acc_early = acc_full + 4;
+  uint64_t* drain = acc_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 4);
+      mbar_init(smem_u32(&acc_early[b]), 4);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;  // global stage counter across tiles
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(p, t, tm, tn);
+        const int m0 = tm * kBM, n0 = tn * BN;
+        for (int kt = 0; kt < p.num_kt; ++kt, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+          if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word,
+                         kErrWaitSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          int nkb = p.ka - kt * kKBlocksPerStage;
+          if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+          const uint32_t sf_bytes = static_cast<uint32_t>(nkb) * 512u;
+          int nsfb = 0;
+          for (int jb = 0; jb < (BN + 127) / 128; ++jb)
+            if (n0 / 128 + jb < p.sfb_rowblocks) ++nsfb;
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes + sf_bytes * (1 + nsfb));
+          tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * kBKBytes, m0, fb);
+          tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes, n0, fb);
+          bulk_load(smem_u32(sSFA + s * C::kSfaBytes),
+                    p.sfa + (static_cast<size_t>(tm) * p.ka + kt * kKBlocksPerStage) * 512,
+                    sf_bytes, fb);
+          for (int jb = 0; jb < nsfb; ++jb) {
+            const size_t rb = static_cast<size_t>(n0 / 128 + jb);
+            bulk_load(smem_u32(sSFB + s * C::kSfbBytes + jb * kKBlocksPerStage * 512),
+                      p.sfb + (rb * p.ka + kt * kKBlocksPerStage) * 512, sf_bytes, fb);
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: the most recent fill of every stage must land before the CTA exits.
+        for (int back = 1; back <= C::kStages && it - back >= 0; ++back) {
+          const int f = it - back;
+          mbar_wait_drain(smem_u32(&full[f % C::kStages]),
+                          static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_mxf4nvf4(kBM, BN);
+      const uint32_t sfa_t = tmem_base + kSfCol;
+      const uint32_t sfb_t = tmem_base + kSfCol + kKBlocksPerStage * 4;
+      int it = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+        const int b = local & 1;
+        const uint32_t u = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(smem_u32(&acc_empty[b]), (u & 1u) ^ 1u, abort_flag, p.err_word,
+                       kErrWaitAccEmpty)) {
+          ok = false;
+          break;
+        }
+        if (C::kOverlap && local > 0) {
+          const uint32_t up = static_cast<uint32_t>((local - 1) >> 1);
+          if (!mbar_wait(smem_u32(&acc_early[b ^ 1]), up & 1u, abort_flag, p.err_word,
+                         kErrWaitAccEmpty)) {
+            ok = false;
+            break;
+          }
+        }
+        tc_fence_after();
+        const uint32_t acc_t = tmem_base + (b ? C::kAccBase1 : 0);
+        for (int kt = 0; kt < p.num_kt; ++kt, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+          if (!mbar_wait(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word, kErrWaitTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          int nkb = p.ka - kt * kKBlocksPerStage;
+          if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+          const uint32_t a_s = smem_u32(sA + s * C::kABytes);
+          const uint32_t b_s = smem_u32(sB + s * C::kBBytes);
+          const uint32_t sfa_s = smem_u32(sSFA + s * C::kSfaBytes);
+          const uint32_t sfb_s = smem_u32(sSFB + s * C::kSfbBytes);
+          for (int kb = 0; kb < nkb; ++kb) {
+            tc_cp_32x128b_x4(sfa_t + kb * 4, make_sdesc(sfa_s + kb * 512, 16, 128, 0));
+            for (int jb = 0; jb < (BN + 127) / 128; ++jb)
+              tc_cp_32x128b_x4(sfb_t + kb * C::kSfbCols + jb * 4,
+                               make_sdesc(sfb_s + jb * kKBlocksPerStage * 512 + kb * 512, 16,
+                                          128, 0));
+          }
+          for (int kb = 0; kb < nkb; ++kb) {
+            const uint64_t ad = make_sdesc(a_s + kb * 32, 16, 1024, 2);
+            const uint64_t bd = make_sdesc(b_s + kb * 32, 16, 1024, 2);
+            tc_mma_mxf4nvf4(acc_t, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * C::kSfbCols,
+                            (kt > 0 || kb > 0) ? 1u : 0u);
+          }
+          issued = true;
+          tc_commit(smem_u32(&empty[s]));
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&acc_full[b]));
+      }
+      if (!ok && issued) {
+        tc_commit(smem_u32(drain));
+        mbar_wait_drain(smem_u32(drain), 0, p.err_word);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;                 // TMEM lane quadrant of this warp
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      const int b = local & 1;
+      const uint32_t u = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(smem_u32(&acc_full[b]), u & 1u, abort_flag, p.err_word, kErrWaitAccFull))
+        break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      const int row = tm * kBM + row_in_tile;
+      const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             (b ? C::kAccBase1 : 0);
+      for (int ci = 0; ci < C::kChunks; ++ci) {
+        // Drain order: the chunks shared with the other buffer first.
+        int c = ci;
+        if (C::kOverlap && b == 0) c = (ci + C::kChunks - C::kOverlapChunks) % C::kChunks;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(acc_t + c * 32, r);
+        tc_wait_ld();
+        if (C::kOverlap && ci == C::kOverlapChunks - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acc_early[b]));
+        }
+        const int col0 = tn * BN + c * 32;
+        if (row < p.M && col0 < p.N) {
+          const bool full_chunk = col0 + 32 <= p.N;
+          if (p.out_bf16) {
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) +
+                                 static_cast<size_t>(row) * p.ldc + col0;
+            if (full_chunk && (p.ldc % 8) == 0) {
+              uint4* o = reinterpret_cast<uint4*>(out);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                uint4 w;
+                w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * p.alpha,
+                                  __uint_as_float(r[8 * v + 1]) * p.alpha);
+                w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * p.alpha,
+                                  __uint_as_float(r[8 * v + 3]) * p.alpha);
+                w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * p.alpha,
+                                  __uint_as_float(r[8 * v + 5]) * p.alpha);
+                w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * p.alpha,
+                                  __uint_as_float(r[8 * v + 7]) * p.alpha);
+                o[v] = w;
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj)
+                if (col0 + jj < p.N) out[jj] = __float2bfloat16_rn(__uint_as_float(r[jj]) * p.alpha);
+            }
+          } else {
+            float* out = reinterpret_cast<float*>(p.out) + static_cast<size_t>(row) * p.ldc + col0;
+            if (full_chunk && (p.ldc % 4) == 0) {
+              float4* o = reinterpret_cast<float4*>(out);
+#pragma unroll
+              for (int v = 0; v < 8; ++v)
+                o[v] = make_float4(__uint_as_float(r[4 * v + 0]) * p.alpha,
+                                   __uint_as_float(r[4 * v + 1]) * p.alpha,
+                                   __uint_as_float(r[4 * v + 2]) * p.alpha,
+                                   __uint_as_float(r[4 * v + 3]) * p.alpha);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj)
+                if (col0 + jj < p.N) out[jj] = __uint_as_float(r[jj]) * p.alpha;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+// One CTA waits on an mbarrier nothing completes, with a short limit: exercises the
+// timeout path (error word + clean return) without faulting or hanging the GPU.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, uint32_t* err_word) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(smem_u32(&bar), 0)) {
+      if (globaltimer_ns() - t0 > limit_ns) {
+        atomicOr(err_word, kErrTest);
+        break;
+      }
+    }
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// Packed FP4 rows as a 2-D UINT8 tensor [rows][K/2], box {128 bytes, box_rows}, 128-byte
+// swizzle, zero fill out of bounds.
+bool encode_operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows,
+                        std::string* err) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) {
+    set_err(err, "cuTensorMapEncodeTiled unavailable from the driver");
+    return false;
+  }
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBKBytes), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_err(err, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
+    return false;
+  }
+  return true;
+}
+
+struct DeviceState {
+  bool init = false;
+  int sms = 0;
+  int cc_major = 0, cc_minor = 0;
+  bool attr_set[2] = {false, false};
+  uint32_t* err_word = nullptr;
+  // Workspace for canonical -> tcgen05 scale reordering (grown on demand).
+  uint8_t* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+
+std::mutex g_mu;
+std::vector<DeviceState> g_dev;
+
+DeviceState* device_state(std::string* err) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    set_err(err, "cudaGetDevice failed");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (static_cast<int>(g_dev.size()) <= dev) g_dev.resize(dev + 1);
+  DeviceState& d = g_dev[dev];
+  if (!d.init) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+      set_err(err, "cudaGetDeviceProperties failed");
+      return nullptr;
+    }
+    d.sms = prop.multiProcessorCount;
+    d.cc_major = prop.major;
+    d.cc_minor = prop.minor;
+    void* sym = nullptr;
+    if (cudaGetSymbolAddress(&sym, g_device_error) != cudaSuccess) {
+      set_err(err, "cudaGetSymbolAddress(g_device_error) failed");
+      return nullptr;
+    }
+    d.err_word = static_cast<uint32_t*>(sym);
+    d.init = true;
+  }
+  return &d;
+}
+
+template <int BN>
+bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                  DeviceState* ds, cudaStream_t s, std::string* err) {
+  using C = Cfg<BN>;
+  const int idx = BN == 256 ? 1 : 0;
+  if (!ds->attr_set[idx]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_mxf4nvf4_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) {
+      set_err(err, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      return false;
+    }
+    ds->attr_set[idx] = true;
+  }
+  int grid = p.num_tiles < ds->sms ? p.num_tiles : ds->sms;
+  gemm_mxf4nvf4_kernel<BN><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(err, std::string("gemm launch: ") + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+size_t sf_tcgen05_bytes(int rows, int K) {
+  return static_cast<size_t>((rows + 127) / 128) * static_cast<size_t>((K + 63) / 64) * 512;
+}
+
+uint32_t* device_error_word(std::string* err) {
+  DeviceState* ds = device_state(err);
+  return ds ? ds->err_word : nullptr;
+}
+
+bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err) {
+  DeviceState* ds = device_state(err);
+  if (!ds) return false;
+  if (ds->cc_major != 10) {
+    set_err(err, "the b200 backend needs an sm_100 device (found sm_" +
+                     std::to_string(ds->cc_major) + std::to_string(ds->cc_minor) + ")");
+    return false;
+  }
+  if (!op.a_packed || !op.b_packed || !op.a_scales || !op.b_scales) {
+    set_err(err, "null operand pointer");
+    return false;
+  }
+  void* out = op.d ? op.d : static_cast<void*>(op.c);
+  if (!out) {
+    set_err(err, "null output pointer");
+    return false;
+  }
+  if (op.d == nullptr && op.out_dtype != OutDType::F32) {
+    set_err(err, "out_dtype BF16 needs the output in `d`");
+    return false;
+  }
+  if (op.M <= 0 || op.N <= 0 || op.K <= 0) {
+    set_err(err, "M, N and K must be positive");
+    return false;
+  }
+  if (op.K % 32 != 0) {
+    set_err(err, "K must be a multiple of 32 (packed rows must be 16-byte aligned for TMA)");
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(op.a_packed) | reinterpret_cast<uintptr_t>(op.b_packed)) & 15) {
+    set_err(err, "packed operands must be 16-byte aligned");
+    return false;
+  }
+  const uint8_t* sfa = op.a_scales;
+  const uint8_t* sfb = op.b_scales;
+  if (op.sf_layout == SfLayout::Canonical) {
+    const size_t na = sf_tcgen05_bytes(op.M, op.K), nb = sf_tcgen05_bytes(op.N, op.K);
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      if (ds->ws_bytes < na + nb) {
+        if (ds->ws) cudaFree(ds->ws);
+        ds->ws = nullptr;
+        ds->ws_bytes = 0;
+        if (cudaMalloc(&ds->ws, na + nb) != cudaSuccess) {
+          set_err(err, "cudaMalloc of the scale workspace failed");
+          return false;
+        }
+        ds->ws_bytes = na + nb;
+      }
+    }
+    if (!sf_to_tcgen05(op.a_scales, op.M, op.K, ds->ws, s, err)) return false;
+    if (!sf_to_tcgen05(op.b_scales, op.N, op.K, ds->ws + na, s, err)) return false;
+    sfa = ds->ws;
+    sfb = ds->ws + na;
+  }
+  if ((reinterpret_cast<uintptr_t>(sfa) | reinterpret_cast<uintptr_t>(sfb)) & 15) {
+    set_err(err, "tcgen05-layout scales must be 16-byte aligned");
+    return false;
+  }
+  return gemm_dense_tc(op, sfa, sfb, out, s, err);
+}
+
+bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb,
+                   void* out, cudaStream_t s, std::string* err) {
+  DeviceState* ds = device_state(err);
+  if (!ds) return false;
+  int bn = op.tile_n;
+  const int tiles_m = (op.M + kBM - 1) / kBM;
+  if (bn == 0) bn = (static_cast<long>(tiles_m) * ((op.N + 255) / 256) >= ds->sms) ? 256 : 128;
+  if (bn != 128 && bn != 256) {
+    set_err(err, "tile_n must be 128 or 256 for the dense kernel");
+    return false;
+  }
+  GemmParams p;
+  p.sfa = sfa;
+  p.sfb = sfb;
+  p.out = out;
+  p.M = op.M;
+  p.N = op.N;
+  p.K = op.K;
+  p.ldc = op.N;
+  p.alpha = op.a_global * op.b_global;
+  p.out_bf16 = (op.d != nullptr && op.out_dtype == OutDType::BF16) ? 1 : 0;
+  p.tiles_m = tiles_m;
+  p.tiles_n = (op.N + bn - 1) / bn;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = 16;
+  p.ka = (op.K + 63) / 64;
+  p.num_kt = (op.K + 255) / 256;
+  p.sfb_rowblocks = (op.N + 127) / 128;
+  p.err_word = ds->err_word;
+  CUtensorMap ta, tb;
+  if (!encode_operand_map(&ta, op.a_packed, op.M, op.K, kBM, err)) return false;
+  if (!encode_operand_map(&tb, op.b_packed, op.N, op.K, bn, err)) return false;
+  return bn == 256 ? launch_dense<256>(ta, tb, p, ds, s, err)
+                   : launch_dense<128>(ta, tb, p, ds, s, err);
+}
+
+bool wait_selftest(uint64_t limit_ns, std::string* err) {
+  DeviceState* ds = device_state(err);
+  if (!ds) return false;
+  wait_selftest_kernel<<<1, 32>>>(limit_ns, ds->err_word);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(err, std::string("selftest launch: ") + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+}  // namespace nvfp4b200
+
+// src/gemm.h:27-29 signature; registered in launch_gemm (include/gemm.h).
+bool launch_gemm_b200(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err) {
+  if (op.mode == GemmMode::Sparse) return nvfp4b200::gemm_sparse(op, s, err);
+  return nvfp4b200::gemm_dense(op, s, err);
+}

@@ -1,0 +1,43 @@
+// internal.h - declarations shared by the engine's translation units (not installed).
+#pragma once
+
+#include <cstdint>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "gemm.h"
+
+namespace nvfp4b200 {
+
+inline void set_err(std::string* err, const std::string& msg) {
+  if (err) *err = msg;
+}
+
+// ---- GEMM (gemm_b200.cu, gemm_sparse.cu) ---------------------------------------------
+size_t sf_tcgen05_bytes(int rows, int K);
+bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
+// Dense GEMM with scales already in the tcgen05 layout; `out` is op.d or op.c.
+bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb,
+                   void* out, cudaStream_t s, std::string* err);
+bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
+uint32_t* device_error_word(std::string* err);
+bool wait_selftest(uint64_t limit_ns, std::string* err);
+
+// ---- codecs (codec.cu) ---------------------------------------------------------------
+bool fill_uniform(float* out, size_t n, uint64_t seed, cudaStream_t s, std::string* err);
+bool fill_normal(float* out, size_t n, uint64_t seed, cudaStream_t s, std::string* err);
+bool quantize(const float* src, int rows, int cols, float global_scale, uint8_t* packed,
+              uint8_t* scales, uint8_t* scales_tc, cudaStream_t s, std::string* err);
+bool dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                float global_scale, float* out, cudaStream_t s, std::string* err);
+bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStream_t s,
+                   std::string* err);
+
+// ---- roofs (roofs.cu) ----------------------------------------------------------------
+bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, size_t bytes,
+                       int iters, double* gbs, cudaStream_t s, std::string* err);
+bool peak_ladder(int n, int ctas, int iters, int reps, double* tflops, cudaStream_t s,
+                 std::string* err);
+
+}  // namespace nvfp4b200

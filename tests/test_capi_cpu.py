@@ -1,0 +1,66 @@
+"""CPU: the C-ABI library loads and exports exactly what include/nvfp4_b200.h declares."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from nvfp4bench_b200 import api, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(build.LIB):
+        build.build()
+    return api.lib()
+
+
+def declared_symbols():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for f in os.listdir(inc):
+        if not f.endswith(".h"):
+            continue
+        text = open(os.path.join(inc, f)).read()
+        if 'extern "C"' not in text:
+            continue
+        names |= set(re.findall(r"\b(nvfp4_b200_\w+)\s*\(", text))
+    return names
+
+
+def test_exports_every_declared_symbol(lib):
+    decl = declared_symbols()
+    assert decl, "no C-ABI declarations found"
+    assert decl == set(api.EXPORTED)
+    for name in decl:
+        assert hasattr(lib, name), name
+
+
+def test_version_and_sizes(lib):
+    assert "sm_100a" in api.version()
+    assert api.sf_tcgen05_bytes(4096, 4096) == 32 * 64 * 512
+    assert api.sf_tcgen05_bytes(1, 16) == 512
+    assert api.sf_tcgen05_bytes(0, 64) == 0
+
+
+def test_null_args_rejected_without_gpu(lib):
+    buf = C.create_string_buffer(256)
+    rc = lib.nvfp4_b200_gemm(None, None, buf, 256)
+    assert rc == 1 and b"null" in buf.value
+
+
+def test_bad_mode_rejected_without_gpu(lib):
+    args = api.GemmArgs()
+    args.mode = 7
+    buf = C.create_string_buffer(256)
+    assert lib.nvfp4_b200_gemm(C.byref(args), None, buf, 256) == 1
+    assert b"mode" in buf.value
+
+
+def test_reference_backend_slots_report_not_built():
+    """The C++ interface keeps the reference's KernelKind values (src/common.h:33)."""
+    text = open(os.path.join(ROOT, "include", "gemm.h")).read()
+    for k in ("Stub", "Cutlass", "Custom", "B200"):
+        assert f"KernelKind::{k}" in text

@@ -1,0 +1,99 @@
+"""GPU: the tcgen05 GEMM against the CPU oracle (src/reference.cu restated) through the C ABI.
+
+Criterion (north_star): max |err| <= 1e-3 * max |C_ref| with FP32 output; BF16 output adds
+half a BF16 ulp of |C_ref| for the final rounding.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import check_gemm, make_operand, oracle_dequant, run_gemm
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _case(api, orc, M, N, K, seed=11, dist="normal", out=torch.float32, ga=1.0, gb=1.0, **kw):
+    _, a = make_operand(api, M, K, seed, dist, ga)
+    _, b = make_operand(api, N, K, seed ^ 0xABCDEF, dist, gb)
+    c = run_gemm(api, a, b, M, N, K, out_dtype=out, **kw)
+    ref = orc.gemm_nt(oracle_dequant(orc, a), oracle_dequant(orc, b))
+    return check_gemm(c.float().cpu().numpy(), ref, bf16=(out == torch.bfloat16))
+
+
+def test_int_gemm_known_answer(api):
+    """The reference's exact-integer self-check (src/gemm_warp_mxf4.cu:124-157): codes 0..7,
+    unit scales (UE4M3 0x38 = 1.0); the answer is exact, so the error must be 0."""
+    g = np.load(os.path.join(GOLD, "int_gemm.npz"))
+    ca, cb = g["codes_a"], g["codes_b_kn"].T.copy()
+
+    def pack(codes):
+        return torch.from_numpy((codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)).cuda()
+
+    sc = torch.full((128, 8), 0x38, dtype=torch.uint8, device="cuda")
+    out = torch.empty((128, 128), dtype=torch.float32, device="cuda")
+    api.gemm(pack(ca), sc, pack(cb), sc, 128, 128, 128, out, sf_layout=api.SF_CANONICAL)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), g["c"])
+
+
+def test_c1_1024_cubed_fp32(api, orc):
+    """M=N=K=1024, N(0,1) operands, FP32 output."""
+    _case(api, orc, 1024, 1024, 1024)
+
+
+@pytest.mark.parametrize("tile_n", [128, 256])
+def test_tiles_and_bf16(api, orc, tile_n):
+    _case(api, orc, 512, 768, 1024, out=torch.bfloat16, tile_n=tile_n)
+    _case(api, orc, 384, 512, 512, tile_n=tile_n)
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 64), (128, 256, 256), (200, 300, 320), (1, 16, 64),
+                                   (129, 257, 288), (17, 1000, 96), (640, 200, 2048)])
+def test_ragged_shapes(api, orc, shape):
+    M, N, K = shape
+    _case(api, orc, M, N, K, seed=M + N + K)
+
+
+def test_canonical_layout_and_global_scales(api, orc):
+    _case(api, orc, 256, 384, 512, sf_layout=api.SF_CANONICAL, ga=0.5, gb=3.0)
+    _case(api, orc, 256, 384, 512, dist="uniform", ga=2.0, gb=0.25, out=torch.bfloat16)
+
+
+def test_many_tiles_persistent(api, orc):
+    """More tiles than SMs: the persistent loop, both accumulator buffers and their overlap."""
+    _case(api, orc, 2048, 4096, 512, out=torch.bfloat16, tile_n=256)
+    _case(api, orc, 2048, 2048, 512, tile_n=128)
+
+
+def test_c2_shape_sampled_rows(api, orc):
+    """BASELINE config 2 (4096 x 14336 x 4096, BF16 out): 96 sampled rows vs the oracle."""
+    M, N, K = 4096, 14336, 4096
+    _, a = make_operand(api, M, K, 1234)
+    _, b = make_operand(api, N, K, 1234 ^ 0xABCDEF)
+    c = run_gemm(api, a, b, M, N, K, out_dtype=torch.bfloat16)
+    rows = np.unique(np.concatenate([np.arange(0, M, 97), [M - 1, 127, 128, 255]]))[:96]
+    adq = oracle_dequant(orc, a)
+    bdq = oracle_dequant(orc, b)
+    ref = orc.gemm_nt_rows(adq, bdq, rows)
+    check_gemm(c[torch.from_numpy(rows).long().cuda()].float().cpu().numpy(), ref, bf16=True)
+
+
+def test_repeat_is_deterministic(api):
+    M, N, K = 512, 1024, 1024
+    _, a = make_operand(api, M, K, 3)
+    _, b = make_operand(api, N, K, 4)
+    c1 = run_gemm(api, a, b, M, N, K)
+    c2 = run_gemm(api, a, b, M, N, K)
+    assert torch.equal(c1, c2)
+
+
+def test_rejects_bad_k(api):
+    x = torch.zeros((128, 48), device="cuda")
+    t = api.quantize(x)
+    out = torch.empty((128, 128), device="cuda")
+    with pytest.raises(api.Nvfp4Error):
+        api.gemm(t.packed, t.scales, t.packed, t.scales, 128, 128, 48, out,
+                 sf_layout=api.SF_CANONICAL)

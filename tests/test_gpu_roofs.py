@@ -1,0 +1,30 @@
+"""GPU: the roofline probes and the bounded-wait failure path (no fault, no hang)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_bounded_wait_times_out_cleanly(api):
+    word = api.wait_selftest(20_000_000)  # 20 ms limit on a barrier nothing completes
+    assert word & (1 << 5)
+    assert api.device_error() == 0       # cleared by the self test
+    x = api.fill_uniform(4, 16, 1)       # the context is still usable
+    torch.cuda.synchronize()
+    assert x.abs().max().item() <= 1.0
+
+
+def test_hbm_probe(api):
+    n = 1 << 30
+    a = torch.empty(n, dtype=torch.uint8, device="cuda")
+    b = torch.empty(n, dtype=torch.uint8, device="cuda")
+    gbs = api.measure_bandwidth(0, a, b, None, n, iters=5)
+    assert 2000 < gbs < 9000
+    gbs_r = api.measure_bandwidth(1, a, b, None, n, iters=5)
+    assert 2000 < gbs_r < 9000
+
+
+def test_peak_ladder(api):
+    tf = api.peak(256, 148, 2048, 3)
+    assert tf > 1000  # TFLOP/s; dense FP4 nominal is about 9000 at boost clock
+    assert api.device_error() == 0
