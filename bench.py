@@ -203,8 +203,9 @@ def run_b200(args, rank, world, local_rank):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
-    # Measured roofs for this run (tcgen05 FP4 ladder, HBM copy).
-    peak_tf = api.peak(256, torch.cuda.get_device_properties(dev).multi_processor_count, 4096, 5)
+    # Measured compute roof for this run (tcgen05 FP4 ladder).
+    peak_tf = None if args.kernel_only else api.peak(
+        256, torch.cuda.get_device_properties(dev).multi_processor_count, 4096, 5)
 
     def step():
         api.launch(gargs)
@@ -248,6 +249,12 @@ def run_b200(args, rank, world, local_rank):
     flops = 2.0 * M * N * K
     value = world * flops / (mean_ms * 1e-3) / 1e12
     achieved = flops / (mean_ms * 1e-3) / 1e12
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"metric": "nvfp4_gemm_tflops", "value": value, "unit": "TFLOP/s",
+                              "ms_per_step": mean_ms, "kernel_only": True,
+                              "config": {"workload": desc}}), flush=True)
+        return 0
 
     # Reference-style timing (src/bench.cu:90-105): per-launch events, no flush, burst=min,
     # sustained=median of 50.
@@ -358,6 +365,9 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-s", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time the device steps only (no ladder, e2e, reference-style timing or "
+                         "CPU baseline): the command profiled under ncu")
     args = ap.parse_args(argv)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
