@@ -16,7 +16,8 @@ import torch
 
 from . import build as _build
 
-LIB_PATH = _build.LIB
+# NVFP4_B200_LIB overrides the library path (to compare two builds side by side).
+LIB_PATH = os.environ.get("NVFP4_B200_LIB", _build.LIB)
 
 MODE_DENSE, MODE_SPARSE24 = 0, 1
 SF_CANONICAL, SF_TCGEN05 = 0, 1

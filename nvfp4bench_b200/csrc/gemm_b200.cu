@@ -6,20 +6,30 @@
 // launch_gemm_custom (src/gemm.h:27-29) and honours its ownership and error rules
 // (src/gemm.h:25-26: return false + message, never throw, never exit, async on the stream).
 //
-// Kernel design (one persistent CTA per SM, 192 threads):
+// Kernel design (one persistent CTA per SM, 320 threads):
 //   warp 0      TMA producer: per K-stage, two tiled TMA loads (A 128 x 256 FP4, B BN x 256
 //               FP4, both 128-byte-swizzled K-major) and 1-D bulk copies of the scale atoms,
 //               all completing on one mbarrier ("full"). No multicast.
-//   warp 1      MMA issuer (one lane): tcgen05.cp of the stage's scale atoms into TMEM, then
-//               four tcgen05.mma kind::mxf4nvf4 block_scale (M=128, N=BN, K=64 each);
-//               tcgen05.commit frees the smem stage ("empty") and, per tile, publishes the
+//   warp 1      MMA issuer (one lane): per K-stage, four tcgen05.mma kind::mxf4nvf4
+//               block_scale (M=128, N=BN, K=64) back to back. tcgen05.commit frees the scale
+//               slot ("sf_empty") and the smem stage ("empty") and, per tile, publishes the
 //               accumulator ("acc_full").
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, scale by alpha, convert to
 //               FP32/BF16, store. Warp w reads TMEM lane quadrant w % 4.
+//   warps 6..9  scale writers: per K-stage, each copies the stage's scale atoms from shared
+//               memory into a ring of three scale slots in TMEM with tcgen05.st (one batched
+//               store per stage: a cross-warp mbarrier round trip costs ~390 cycles, so a
+//               per-K-block handshake would be slower than the 128-cycle MMA it feeds). Each warp writes its
+//               own 32-lane quadrant, so the four quadrants hold identical copies: the layout
+//               the block-scaled MMA reads. tcgen05.cp would do the same copy on the tensor
+//               pipe, in series with the MMAs (measured on B200: 4 MMAs of a stage take 512
+//               cycles, 980 with the stage's 12 copies); tcgen05.st from these warps runs
+//               beside the MMAs.
 // Two accumulator buffers let the epilogue of tile i overlap the MMAs of tile i+1. With
-// BN = 256 the two 256-column buffers and the 64 scale columns do not fit the 512 TMEM
-// columns side by side, so buffer 1 starts at column 192: the 64 shared columns are drained
-// first and released early ("acc_early"), the rest of the buffer afterwards.
+// BN = 256 the two 256-column buffers and the 144 scale columns do not fit the 512 TMEM
+// columns side by side, so buffer 1 starts at column 112: the epilogue loads the 5 chunks
+// that hold the 144 shared columns first, releases them ("acc_early") as soon as they are in registers, and drains
+// the rest afterwards.
 //
 // Every mbarrier wait is bounded (ptx.cuh); a timeout sets the device error word, all roles
 // leave their loops, in-flight copies and MMAs are drained with bounded waits, TMEM is freed
@@ -47,10 +57,12 @@ namespace {
 constexpr int kBM = 128;          // rows of A per tile (= TMEM lanes)
 constexpr int kBKBytes = 128;     // one K-stage = 256 FP4 = 128 bytes per row (one swizzle atom)
 constexpr int kKBlocksPerStage = 4;  // MMA K = 64 -> 4 MMAs per stage
-constexpr int kNumThreads = 192;
-constexpr int kEpiWarp0 = 2;
+constexpr int kNumThreads = 320;
 constexpr int kTmemCols = 512;
-constexpr int kSfCol = 448;       // scale factors live in TMEM columns [448, 512)
+constexpr int kSfSlots = 3;       // ring of per-stage scale slots in TMEM
+constexpr int kSfSlotCols = 48;   // SFA at +4*kb (16 columns), SFB at +16 + 8*kb (32 columns)
+constexpr int kSfbOff = 16;
+constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368
 
 template <int BN>
 struct Cfg {
@@ -60,16 +72,19 @@ struct Cfg {
   static constexpr int kSfbBytes = (BN + 127) / 128 * kKBlocksPerStage * 512;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kStages = (BN == 256) ? 4 : 6;
-  static constexpr int kBarBytes = 256;
+  static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
   // TMEM: accumulator buffers and which 32-column chunks are shared between them.
-  static constexpr int kAccBase1 = (BN == 256) ? 192 : BN;
+  static constexpr int kAccBase1 = (BN == 256) ? kSfCol - 256 : BN;  // 112 for BN = 256
   static constexpr int kChunks = BN / 32;
   static constexpr bool kOverlap = (BN == 256);
-  static constexpr int kOverlapChunks = 2;  // columns [192, 256)
-  static constexpr int kSfbCols = (BN + 127) / 128 * 4;  // per K-block
+  // Buffer 0 chunks 3..7 and buffer 1 chunks 0..4 hold the shared columns [112, 256).
+  static constexpr int kOverlapChunks = 5;
+  static constexpr int kSfbAtoms = (BN + 127) / 128;
+  static constexpr int kSfbColsPerKb = kSfbAtoms * 4;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kAccBase1 + BN <= kSfCol, "TMEM budget");
+  static_assert(!kOverlap || (kAccBase1 == 112 && kOverlapChunks == 5), "overlap chunks");
 };
 
 struct GemmParams {
@@ -110,6 +125,65 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Scale one 32-column chunk of a row by alpha and store it (vector stores when the chunk is
+// whole and the row is aligned, element stores at the ragged edges).
+__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int row,
+                                            int col0) {
+  if (row >= p.M || col0 >= p.N) return;
+  const bool full_chunk = col0 + 32 <= p.N;
+  if (p.out_bf16) {
+    __nv_bfloat16* out =
+        reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ldc + col0;
+    if (full_chunk && (p.ldc % 8) == 0) {
+      uint4* o = reinterpret_cast<uint4*>(out);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * p.alpha, __uint_as_float(r[8 * v + 1]) * p.alpha);
+        w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * p.alpha, __uint_as_float(r[8 * v + 3]) * p.alpha);
+        w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * p.alpha, __uint_as_float(r[8 * v + 5]) * p.alpha);
+        w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * p.alpha, __uint_as_float(r[8 * v + 7]) * p.alpha);
+        o[v] = w;
+      }
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj)
+        if (col0 + jj < p.N) out[jj] = __float2bfloat16_rn(__uint_as_float(r[jj]) * p.alpha);
+    }
+  } else {
+    float* out = reinterpret_cast<float*>(p.out) + static_cast<size_t>(row) * p.ldc + col0;
+    if (full_chunk && (p.ldc % 4) == 0) {
+      float4* o = reinterpret_cast<float4*>(out);
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        o[v] = make_float4(__uint_as_float(r[4 * v + 0]) * p.alpha, __uint_as_float(r[4 * v + 1]) * p.alpha,
+                           __uint_as_float(r[4 * v + 2]) * p.alpha, __uint_as_float(r[4 * v + 3]) * p.alpha);
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj)
+        if (col0 + jj < p.N) out[jj] = __uint_as_float(r[jj]) * p.alpha;
+    }
+  }
+}
+
+// Load CNT chunks of the accumulator with back-to-back tcgen05.ld and one wait, optionally
+// release them (arrive on `early_bar`) as soon as they are in registers, then store them.
+template <int CNT>
+__device__ __forceinline__ void epi_group(const GemmParams& p, uint32_t acc_t, const int (&cs)[CNT],
+                                          int row, int col_base, uint32_t early_bar) {
+  uint32_t r[CNT][32];
+#pragma unroll
+  for (int g = 0; g < CNT; ++g) tmem_ld_32x32b_x32(acc_t + cs[g] * 32, r[g]);
+  tc_wait_ld();
+  if (early_bar) {
+    tc_fence_before();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(early_bar);
+  }
+#pragma unroll
+  for (int g = 0; g < CNT; ++g) store_chunk(p, r[g], row, col_base + cs[g] * 32);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_mxf4nvf4_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -128,7 +202,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* acc_full = bars + 2 * C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* acc_early = acc_full + 4;
-  uint64_t* drain = acc_full + 6;
+  uint64_t* sf_full = acc_full + 6;
+  uint64_t* sf_empty = sf_full + kSfSlots;
+  uint64_t* drain = sf_empty + kSfSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -144,6 +220,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&acc_empty[b]), 4);
       mbar_init(smem_u32(&acc_early[b]), 4);
+    }
+    for (int j = 0; j < kSfSlots; ++j) {
+      mbar_init(smem_u32(&sf_full[j]), 4);
+      mbar_init(smem_u32(&sf_empty[j]), 1);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -210,9 +290,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc_mxf4nvf4(kBM, BN);
-      const uint32_t sfa_t = tmem_base + kSfCol;
-      const uint32_t sfb_t = tmem_base + kSfCol + kKBlocksPerStage * 4;
-      int it = 0;
+      int it = 0;   // stage counter (also the position in the scale slot ring)
       int local = 0;
       bool ok = true;
       bool issued = false;
@@ -234,10 +312,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         tc_fence_after();
         const uint32_t acc_t = tmem_base + (b ? C::kAccBase1 : 0);
-        for (int kt = 0; kt < p.num_kt; ++kt, ++it) {
+        for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
           const int s = it % C::kStages;
           const uint32_t j = static_cast<uint32_t>(it / C::kStages);
           if (!mbar_wait(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word, kErrWaitTmaFull)) {
+            ok = false;
+            break;
+          }
+          const int slot = it % kSfSlots;
+          if (!mbar_wait(smem_u32(&sf_full[slot]), static_cast<uint32_t>(it / kSfSlots) & 1u,
+                         abort_flag, p.err_word, kErrWaitSfFull)) {
             ok = false;
             break;
           }
@@ -246,22 +330,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
           const uint32_t a_s = smem_u32(sA + s * C::kABytes);
           const uint32_t b_s = smem_u32(sB + s * C::kBBytes);
-          const uint32_t sfa_s = smem_u32(sSFA + s * C::kSfaBytes);
-          const uint32_t sfb_s = smem_u32(sSFB + s * C::kSfbBytes);
-          for (int kb = 0; kb < nkb; ++kb) {
-            tc_cp_32x128b_x4(sfa_t + kb * 4, make_sdesc(sfa_s + kb * 512, 16, 128, 0));
-            for (int jb = 0; jb < (BN + 127) / 128; ++jb)
-              tc_cp_32x128b_x4(sfb_t + kb * C::kSfbCols + jb * 4,
-                               make_sdesc(sfb_s + jb * kKBlocksPerStage * 512 + kb * 512, 16,
-                                          128, 0));
-          }
+          const uint32_t sf_t = tmem_base + kSfCol + slot * kSfSlotCols;
           for (int kb = 0; kb < nkb; ++kb) {
             const uint64_t ad = make_sdesc(a_s + kb * 32, 16, 1024, 2);
             const uint64_t bd = make_sdesc(b_s + kb * 32, 16, 1024, 2);
-            tc_mma_mxf4nvf4(acc_t, ad, bd, idesc, sfa_t + kb * 4, sfb_t + kb * C::kSfbCols,
-                            (kt > 0 || kb > 0) ? 1u : 0u);
+            tc_mma_mxf4nvf4(acc_t, ad, bd, idesc, sf_t + kb * 4,
+                            sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
           }
           issued = true;
+          tc_commit(smem_u32(&sf_empty[slot]));
           tc_commit(smem_u32(&empty[s]));
         }
         if (!ok) break;
@@ -270,6 +347,55 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (!ok && issued) {
         tc_commit(smem_u32(drain));
         mbar_wait_drain(smem_u32(drain), 0, p.err_word);
+      }
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------ scale writers
+    // In an atom, lane l's 16 bytes are 4 words; word g holds the 4 K-scales of row 32g + l.
+    // Slot columns: SFA K-block kb's words at +4*kb, SFB atom jb of K-block kb at
+    // +16 + kb*(4*atoms) + 4*jb. K-blocks past the end of K keep stale words no MMA reads.
+    const int q = warp & 3;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
+        const int s = it % C::kStages;
+        const int slot = it % kSfSlots;
+        if (!mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>(it / C::kStages) & 1u, abort_flag,
+                       p.err_word, kErrWaitTmaFull)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* sfa_s = sSFA + s * C::kSfaBytes + lane * 16;
+        const uint8_t* sfb_s = sSFB + s * C::kSfbBytes + lane * 16;
+        uint32_t va[16], vb[32];
+#pragma unroll
+        for (int kb = 0; kb < kKBlocksPerStage; ++kb) {
+          const uint4 w = *reinterpret_cast<const uint4*>(sfa_s + kb * 512);
+          va[4 * kb + 0] = w.x; va[4 * kb + 1] = w.y; va[4 * kb + 2] = w.z; va[4 * kb + 3] = w.w;
+#pragma unroll
+          for (int jb = 0; jb < C::kSfbAtoms; ++jb) {
+            const uint4 x =
+                *reinterpret_cast<const uint4*>(sfb_s + jb * kKBlocksPerStage * 512 + kb * 512);
+            const int o = kb * C::kSfbColsPerKb + 4 * jb;
+            vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
+          }
+        }
+        if (!mbar_wait(smem_u32(&sf_empty[slot]), (static_cast<uint32_t>(it / kSfSlots) & 1u) ^ 1u,
+                       abort_flag, p.err_word, kErrWaitSfEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sf_t = lane_base + kSfCol + slot * kSfSlotCols;
+        tmem_st_32x32b_x16(sf_t, va);
+        tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
+        if (C::kSfbAtoms == 2) tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sf_full[slot]));
       }
     }
   } else {
@@ -286,62 +412,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int tm, tn;
       tile_coords(p, t, tm, tn);
       const int row = tm * kBM + row_in_tile;
+      const int col_base = tn * BN;
       const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              (b ? C::kAccBase1 : 0);
-      for (int ci = 0; ci < C::kChunks; ++ci) {
-        // Drain order: the chunks shared with the other buffer first.
-        int c = ci;
-        if (C::kOverlap && b == 0) c = (ci + C::kChunks - C::kOverlapChunks) % C::kChunks;
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(acc_t + c * 32, r);
-        tc_wait_ld();
-        if (C::kOverlap && ci == C::kOverlapChunks - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&acc_early[b]));
-        }
-        const int col0 = tn * BN + c * 32;
-        if (row < p.M && col0 < p.N) {
-          const bool full_chunk = col0 + 32 <= p.N;
-          if (p.out_bf16) {
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) +
-                                 static_cast<size_t>(row) * p.ldc + col0;
-            if (full_chunk && (p.ldc % 8) == 0) {
-              uint4* o = reinterpret_cast<uint4*>(out);
+      if (C::kOverlap) {
+        // The columns shared with the other buffer: buffer 0's chunks 3..7, buffer 1's
+        // chunks 0..4. Load them first and release them as soon as they are in registers.
+        const int o = b ? 0 : 3;
+        const int rest = b ? 5 : 0;
+        const int g0[3] = {o, o + 1, o + 2}, g1[2] = {o + 3, o + 4};
+        epi_group<3>(p, acc_t, g0, row, col_base, 0);
+        epi_group<2>(p, acc_t, g1, row, col_base, smem_u32(&acc_early[b]));
+        const int g2[2] = {rest, rest + 1}, g3[1] = {rest + 2};
+        epi_group<2>(p, acc_t, g2, row, col_base, 0);
+        epi_group<1>(p, acc_t, g3, row, col_base, 0);
+      } else {
 #pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                uint4 w;
-                w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * p.alpha,
-                                  __uint_as_float(r[8 * v + 1]) * p.alpha);
-                w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * p.alpha,
-                                  __uint_as_float(r[8 * v + 3]) * p.alpha);
-                w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * p.alpha,
-                                  __uint_as_float(r[8 * v + 5]) * p.alpha);
-                w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * p.alpha,
-                                  __uint_as_float(r[8 * v + 7]) * p.alpha);
-                o[v] = w;
-              }
-            } else {
-#pragma unroll
-              for (int jj = 0; jj < 32; ++jj)
-                if (col0 + jj < p.N) out[jj] = __float2bfloat16_rn(__uint_as_float(r[jj]) * p.alpha);
-            }
-          } else {
-            float* out = reinterpret_cast<float*>(p.out) + static_cast<size_t>(row) * p.ldc + col0;
-            if (full_chunk && (p.ldc % 4) == 0) {
-              float4* o = reinterpret_cast<float4*>(out);
-#pragma unroll
-              for (int v = 0; v < 8; ++v)
-                o[v] = make_float4(__uint_as_float(r[4 * v + 0]) * p.alpha,
-                                   __uint_as_float(r[4 * v + 1]) * p.alpha,
-                                   __uint_as_float(r[4 * v + 2]) * p.alpha,
-                                   __uint_as_float(r[4 * v + 3]) * p.alpha);
-            } else {
-#pragma unroll
-              for (int jj = 0; jj < 32; ++jj)
-                if (col0 + jj < p.N) out[jj] = __uint_as_float(r[jj]) * p.alpha;
-            }
-          }
+        for (int c = 0; c < C::kChunks; c += 2) {
+          const int g[2] = {c, c + 1};
+          epi_group<2>(p, acc_t, g, row, col_base, 0);
         }
       }
       tc_fence_before();

@@ -1,6 +1,6 @@
 // ptx.cuh - thin inline-PTX wrappers for the sm_100a features the engine uses:
 // mbarriers, TMA (cp.async.bulk / cp.async.bulk.tensor, never with cluster multicast),
-// and the 5th-generation tensor-core family tcgen05 (alloc, cp, mma, commit, ld).
+// and the 5th-generation tensor-core family tcgen05 (alloc, cp, mma, commit, ld, st).
 //
 // Every wait is bounded: a waiter polls %globaltimer and, after `kWaitLimitNs`, records an
 // error code in the kernel's error word and in a shared-memory abort flag so that every
@@ -22,6 +22,8 @@ enum DeviceError : uint32_t {
   kErrWaitDrain = 1u << 4,       // a role timed out draining its in-flight work on abort
   kErrTest = 1u << 5,            // the deliberate timeout of the bounded-wait self test
   kErrBadLaunch = 1u << 6,       // kernel launched with an inconsistent configuration
+  kErrWaitSfFull = 1u << 7,      // MMA warp timed out waiting for a scale slot to be written
+  kErrWaitSfEmpty = 1u << 8,     // scale writers timed out waiting for a slot to be freed
 };
 
 // One second: a healthy wait in these kernels lasts microseconds.
@@ -74,16 +76,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with parity `parity` to complete. Returns false (after
-// recording `code`) on timeout or when another role already aborted the CTA.
+// recording `code`) on timeout or when another role already aborted the CTA. The timer is
+// read only once every 1024 polls: a %globaltimer read costs far more than a poll, and
+// reading it on every slow wait was measured to dominate the pipeline's handshakes.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           uint32_t* err_word, uint32_t code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u) {
+    if ((it & 1023u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
         *abort_flag = 1;
         if (err_word) atomicOr(err_word, code);
         return false;
@@ -194,6 +200,30 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
+}
+
+// Thread i of the warp writes TMEM lane (base+i): 4 / 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,
+                                                  uint32_t d) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(a),
+               "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // ---- descriptors ---------------------------------------------------------------------
