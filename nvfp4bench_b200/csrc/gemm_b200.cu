@@ -15,7 +15,10 @@
 //               slot ("sf_empty") and the smem stage ("empty") and, per tile, publishes the
 //               accumulator ("acc_full").
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, scale by alpha, convert to
-//               FP32/BF16, store. Warp w reads TMEM lane quadrant w % 4.
+//               FP32/BF16, write the 32 x 32 chunk into a swizzled, double-buffered shared
+//               tile and store it with one TMA tensor store (clipped at the matrix edges).
+//               Warp w reads TMEM lane quadrant w % 4. Outputs whose row pitch is not a
+//               multiple of 16 bytes fall back to per-thread global stores.
 //   warps 6..9  scale writers: per K-stage, each copies the stage's scale atoms from shared
 //               memory into a ring of three scale slots in TMEM with tcgen05.st (one batched
 //               store per stage: a cross-warp mbarrier round trip costs ~390 cycles, so a
@@ -71,9 +74,11 @@ struct Cfg {
   static constexpr int kSfaBytes = kKBlocksPerStage * 512;       // 2 KB
   static constexpr int kSfbBytes = (BN + 127) / 128 * kKBlocksPerStage * 512;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kStages = (BN == 256) ? 3 : 5;
+  static constexpr int kCBufBytes = 32 * 32 * 4;                // one FP32 32 x 32 chunk
+  static constexpr int kCBytes = 4 * 2 * kCBufBytes;            // 4 warps, double-buffered
   static constexpr int kBarBytes = 512;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
   // TMEM: accumulator buffers and which 32-column chunks are shared between them.
   static constexpr int kAccBase1 = (BN == 256) ? kSfCol - 256 : BN;  // 112 for BN = 256
   static constexpr int kChunks = BN / 32;
@@ -95,6 +100,7 @@ struct GemmParams {
   int ldc;
   float alpha;
   int out_bf16;
+  int tma_store;        // 1: epilogue stores through the C tensor map
   int tiles_m, tiles_n, num_tiles;
   int group_m;
   int ka;               // scale atoms along K = ceil(K/64)
@@ -166,11 +172,55 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
   }
 }
 
+// Per-warp epilogue state for the TMA-store path: two 4 KB staging buffers used in turn.
+struct EpiStage {
+  uint8_t* buf;        // this warp's two buffers
+  uint32_t count;      // chunks stored so far
+  const void* tmap_c;
+  int row0;            // first row of this warp's 32-row slab
+};
+
+// Scale one 32 x 32 chunk (lane = row) by alpha, write it to a staging buffer in the TMA
+// swizzled layout (64-byte swizzle for BF16 rows of 64 bytes, 128-byte for FP32 rows of 128
+// bytes; either way one st.shared.v4 per 16 bytes without bank conflicts) and store it.
+__device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, const uint32_t (&r)[32],
+                                            int col0) {
+  const int lane = threadIdx.x & 31;
+  uint8_t* b = e.buf + (e.count & 1) * 4096;
+  if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer has read it
+  __syncwarp();
+  if (p.out_bf16) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_bf16x2(__uint_as_float(r[8 * j + 0]) * p.alpha, __uint_as_float(r[8 * j + 1]) * p.alpha);
+      w.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]) * p.alpha, __uint_as_float(r[8 * j + 3]) * p.alpha);
+      w.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]) * p.alpha, __uint_as_float(r[8 * j + 5]) * p.alpha);
+      w.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]) * p.alpha, __uint_as_float(r[8 * j + 7]) * p.alpha);
+      *reinterpret_cast<uint4*>(b + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(b + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+          make_float4(__uint_as_float(r[4 * j + 0]) * p.alpha, __uint_as_float(r[4 * j + 1]) * p.alpha,
+                      __uint_as_float(r[4 * j + 2]) * p.alpha, __uint_as_float(r[4 * j + 3]) * p.alpha);
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(e.tmap_c, smem_u32(b), col0, e.row0);
+    bulk_commit_group();
+  }
+  ++e.count;
+}
+
 // Load CNT chunks of the accumulator with back-to-back tcgen05.ld and one wait, optionally
 // release them (arrive on `early_bar`) as soon as they are in registers, then store them.
 template <int CNT>
-__device__ __forceinline__ void epi_group(const GemmParams& p, uint32_t acc_t, const int (&cs)[CNT],
-                                          int row, int col_base, uint32_t early_bar) {
+__device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint32_t acc_t,
+                                          const int (&cs)[CNT], int row, int col_base,
+                                          uint32_t early_bar) {
   uint32_t r[CNT][32];
 #pragma unroll
   for (int g = 0; g < CNT; ++g) tmem_ld_32x32b_x32(acc_t + cs[g] * 32, r[g]);
@@ -181,13 +231,17 @@ __device__ __forceinline__ void epi_group(const GemmParams& p, uint32_t acc_t, c
     if ((threadIdx.x & 31) == 0) mbar_arrive(early_bar);
   }
 #pragma unroll
-  for (int g = 0; g < CNT; ++g) store_chunk(p, r[g], row, col_base + cs[g] * 32);
+  for (int g = 0; g < CNT; ++g) {
+    if (p.tma_store) stage_chunk(p, e, r[g], col_base + cs[g] * 32);
+    else store_chunk(p, r[g], row, col_base + cs[g] * 32);
+  }
 }
 
 template <int BN>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_mxf4nvf4_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                         const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+                         const __grid_constant__ CUtensorMap tmap_b,
+                         const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -196,7 +250,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint8_t* sB = sA + C::kStages * C::kABytes;
   uint8_t* sSFA = sB + C::kStages * C::kBBytes;
   uint8_t* sSFB = sSFA + C::kStages * C::kSfaBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + C::kStages * C::kSfbBytes);
+  uint8_t* sC = sSFB + C::kStages * C::kSfbBytes;  // 1024-aligned: stages are multiples of 1 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::kStages;
   uint64_t* acc_full = bars + 2 * C::kStages;
@@ -230,6 +285,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
+    if (p.tma_store) prefetch_tmap(&tmap_c);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -402,6 +458,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
     const int row_in_tile = q * 32 + lane;
+    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0};
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int b = local & 1;
@@ -413,6 +470,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       tile_coords(p, t, tm, tn);
       const int row = tm * kBM + row_in_tile;
       const int col_base = tn * BN;
+      e.row0 = tm * kBM + q * 32;
       const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              (b ? C::kAccBase1 : 0);
       if (C::kOverlap) {
@@ -421,22 +479,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int o = b ? 0 : 3;
         const int rest = b ? 5 : 0;
         const int g0[3] = {o, o + 1, o + 2}, g1[2] = {o + 3, o + 4};
-        epi_group<3>(p, acc_t, g0, row, col_base, 0);
-        epi_group<2>(p, acc_t, g1, row, col_base, smem_u32(&acc_early[b]));
+        epi_group<3>(p, e, acc_t, g0, row, col_base, 0);
+        epi_group<2>(p, e, acc_t, g1, row, col_base, smem_u32(&acc_early[b]));
         const int g2[2] = {rest, rest + 1}, g3[1] = {rest + 2};
-        epi_group<2>(p, acc_t, g2, row, col_base, 0);
-        epi_group<1>(p, acc_t, g3, row, col_base, 0);
+        epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
+        epi_group<1>(p, e, acc_t, g3, row, col_base, 0);
       } else {
 #pragma unroll
         for (int c = 0; c < C::kChunks; c += 2) {
           const int g[2] = {c, c + 1};
-          epi_group<2>(p, acc_t, g, row, col_base, 0);
+          epi_group<2>(p, e, acc_t, g, row, col_base, 0);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
     }
+    if (lane == 0) bulk_wait_group<0>();  // stores complete before the CTA's smem goes away
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -505,6 +565,30 @@ bool encode_operand_map(CUtensorMap* map, const void* base, int rows, int K, int
   return true;
 }
 
+// Row-major output [M][N] as a 2-D tensor, box 32 x 32 elements, swizzled to match the
+// epilogue's staging layout (64-byte rows for BF16, 128-byte rows for FP32).
+bool encode_output_map(CUtensorMap* map, void* base, int M, int N, bool bf16, std::string* err) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) {
+    set_err(err, "cuTensorMapEncodeTiled unavailable from the driver");
+    return false;
+  }
+  const size_t es = bf16 ? 2 : 4;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(N * es)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                   base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_err(err, "cuTensorMapEncodeTiled (output) failed (code " + std::to_string(static_cast<int>(r)) + ")");
+    return false;
+  }
+  return true;
+}
+
 struct DeviceState {
   bool init = false;
   int sms = 0;
@@ -549,7 +633,8 @@ DeviceState* device_state(std::string* err) {
 }
 
 template <int BN>
-bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  const GemmParams& p,
                   DeviceState* ds, cudaStream_t s, std::string* err) {
   using C = Cfg<BN>;
   const int idx = BN == 256 ? 1 : 0;
@@ -564,7 +649,7 @@ bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams
     ds->attr_set[idx] = true;
   }
   int grid = p.num_tiles < ds->sms ? p.num_tiles : ds->sms;
-  gemm_mxf4nvf4_kernel<BN><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, p);
+  gemm_mxf4nvf4_kernel<BN><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, tc, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_err(err, std::string("gemm launch: ") + cudaGetErrorString(e));
@@ -678,8 +763,15 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   CUtensorMap ta, tb;
   if (!encode_operand_map(&ta, op.a_packed, op.M, op.K, kBM, err)) return false;
   if (!encode_operand_map(&tb, op.b_packed, op.N, op.K, bn, err)) return false;
-  return bn == 256 ? launch_dense<256>(ta, tb, p, ds, s, err)
-                   : launch_dense<128>(ta, tb, p, ds, s, err);
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  const int esize = p.out_bf16 ? 2 : 4;
+  p.tma_store = ((static_cast<size_t>(op.N) * esize) % 16 == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) & 15) == 0)
+                    ? 1 : 0;
+  if (p.tma_store && !encode_output_map(&tc, out, op.M, op.N, p.out_bf16 != 0, err)) return false;
+  return bn == 256 ? launch_dense<256>(ta, tb, tc, p, ds, s, err)
+                   : launch_dense<128>(ta, tb, tc, p, ds, s, err);
 }
 
 bool wait_selftest(uint64_t limit_ns, std::string* err) {
