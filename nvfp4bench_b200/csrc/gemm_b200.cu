@@ -6,7 +6,7 @@
 // launch_gemm_custom (src/gemm.h:27-29) and honours its ownership and error rules
 // (src/gemm.h:25-26: return false + message, never throw, never exit, async on the stream).
 //
-// Kernel design (one persistent CTA per SM, 320 threads):
+// Kernel design (one persistent CTA per SM, 448 threads):
 //   warp 0      TMA producer: per K-stage, two tiled TMA loads (A 128 x 256 FP4, B BN x 256
 //               FP4, both 128-byte-swizzled K-major) and 1-D bulk copies of the scale atoms,
 //               all completing on one mbarrier ("full"). No multicast.
@@ -19,7 +19,9 @@
 //               tile and store it with one TMA tensor store (clipped at the matrix edges).
 //               Warp w reads TMEM lane quadrant w % 4. Outputs whose row pitch is not a
 //               multiple of 16 bytes fall back to per-thread global stores.
-//   warps 6..9  scale writers: per K-stage, each copies the stage's scale atoms from shared
+//   warps 6..13 scale writers, two per TMEM quadrant taking even and odd stages in turn
+//               (one writer's per-stage latency exceeds a stage's 512 MMA cycles): per K-stage,
+//               each copies the stage's scale atoms from shared
 //               memory into a ring of three scale slots in TMEM with tcgen05.st (one batched
 //               store per stage: a cross-warp mbarrier round trip costs ~390 cycles, so a
 //               per-K-block handshake would be slower than the 128-cycle MMA it feeds). Each warp writes its
@@ -60,7 +62,8 @@ namespace {
 constexpr int kBM = 128;          // rows of A per tile (= TMEM lanes)
 constexpr int kBKBytes = 128;     // one K-stage = 256 FP4 = 128 bytes per row (one swizzle atom)
 constexpr int kKBlocksPerStage = 4;  // MMA K = 64 -> 4 MMAs per stage
-constexpr int kNumThreads = 320;
+constexpr int kNumThreads = 448;  // 14 warps
+constexpr int kWriterGroups = 2;  // scale writers: two warps per TMEM quadrant, even/odd stages
 constexpr int kTmemCols = 512;
 constexpr int kSfSlots = 3;       // ring of per-stage scale slots in TMEM
 constexpr int kSfSlotCols = 48;   // SFA at +4*kb (16 columns), SFB at +16 + 8*kb (32 columns)
@@ -83,13 +86,13 @@ struct Cfg {
   static constexpr int kAccBase1 = (BN == 256) ? kSfCol - 256 : BN;  // 112 for BN = 256
   static constexpr int kChunks = BN / 32;
   static constexpr bool kOverlap = (BN == 256);
-  // Buffer 0 chunks 3..7 and buffer 1 chunks 0..4 hold the shared columns [112, 256).
-  static constexpr int kOverlapChunks = 5;
+  // Buffer 0's last and buffer 1's first kOverlapChunks chunks hold the shared columns.
+  static constexpr int kOverlapChunks = (256 - kAccBase1 + 31) / 32;
   static constexpr int kSfbAtoms = (BN + 127) / 128;
   static constexpr int kSfbColsPerKb = kSfbAtoms * 4;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kAccBase1 + BN <= kSfCol, "TMEM budget");
-  static_assert(!kOverlap || (kAccBase1 == 112 && kOverlapChunks == 5), "overlap chunks");
+  static_assert(!kOverlap || (kOverlapChunks >= 4 && kOverlapChunks <= 6), "overlap chunks");
 };
 
 struct GemmParams {
@@ -106,6 +109,7 @@ struct GemmParams {
   int ka;               // scale atoms along K = ceil(K/64)
   int num_kt;           // K-stages = ceil(K/256)
   int sfb_rowblocks;    // ceil(N/128)
+  int sfa_rowblocks;    // ceil(M/128)
   uint32_t* err_word;
 };
 
@@ -217,7 +221,7 @@ __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, co
 
 // Load CNT chunks of the accumulator with back-to-back tcgen05.ld and one wait, optionally
 // release them (arrive on `early_bar`) as soon as they are in registers, then store them.
-template <int CNT>
+template <int CNT, bool kRemote = false>
 __device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint32_t acc_t,
                                           const int (&cs)[CNT], int row, int col_base,
                                           uint32_t early_bar) {
@@ -228,12 +232,42 @@ __device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint
   if (early_bar) {
     tc_fence_before();
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(early_bar);
+    if ((threadIdx.x & 31) == 0) {
+      if (kRemote) mbar_arrive_cluster(early_bar);
+      else mbar_arrive(early_bar);
+    }
   }
 #pragma unroll
   for (int g = 0; g < CNT; ++g) {
     if (p.tma_store) stage_chunk(p, e, r[g], col_base + cs[g] * 32);
     else store_chunk(p, r[g], row, col_base + cs[g] * 32);
+  }
+}
+
+// Drain a 256-column accumulator whose first (buffer 1) or last (buffer 0) OV chunks are
+// shared with the other buffer: those chunks first, released on `early_bar` once they are in
+// registers, then the rest.
+template <int OV, bool kRemote>
+__device__ __forceinline__ void drain_overlapped(const GemmParams& p, EpiStage& e, uint32_t acc_t,
+                                                 int b, int row, int col_base, uint32_t early_bar) {
+  const int o = b ? 0 : 8 - OV;
+  const int rest = b ? OV : 0;
+  const int g0[3] = {o, o + 1, o + 2};
+  epi_group<3>(p, e, acc_t, g0, row, col_base, 0);
+  if constexpr (OV == 6) {
+    const int g1[3] = {o + 3, o + 4, o + 5}, g2[2] = {rest, rest + 1};
+    epi_group<3, kRemote>(p, e, acc_t, g1, row, col_base, early_bar);
+    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
+  } else if constexpr (OV == 5) {
+    const int g1[2] = {o + 3, o + 4}, g2[2] = {rest, rest + 1}, g3[1] = {rest + 2};
+    epi_group<2, kRemote>(p, e, acc_t, g1, row, col_base, early_bar);
+    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
+    epi_group<1>(p, e, acc_t, g3, row, col_base, 0);
+  } else {
+    const int g1[1] = {o + 3}, g2[2] = {rest, rest + 1}, g3[2] = {rest + 2, rest + 3};
+    epi_group<1, kRemote>(p, e, acc_t, g1, row, col_base, early_bar);
+    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
+    epi_group<2>(p, e, acc_t, g3, row, col_base, 0);
   }
 }
 
@@ -411,11 +445,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // Slot columns: SFA K-block kb's words at +4*kb, SFB atom jb of K-block kb at
     // +16 + kb*(4*atoms) + 4*jb. K-blocks past the end of K keep stale words no MMA reads.
     const int q = warp & 3;
+    const int wgroup = (warp - 6) >> 2;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
       for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
+        if ((it % kWriterGroups) != wgroup) continue;
         const int s = it % C::kStages;
         const int slot = it % kSfSlots;
         if (!mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>(it / C::kStages) & 1u, abort_flag,
@@ -476,14 +512,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (C::kOverlap) {
         // The columns shared with the other buffer: buffer 0's chunks 3..7, buffer 1's
         // chunks 0..4. Load them first and release them as soon as they are in registers.
-        const int o = b ? 0 : 3;
-        const int rest = b ? 5 : 0;
-        const int g0[3] = {o, o + 1, o + 2}, g1[2] = {o + 3, o + 4};
-        epi_group<3>(p, e, acc_t, g0, row, col_base, 0);
-        epi_group<2>(p, e, acc_t, g1, row, col_base, smem_u32(&acc_early[b]));
-        const int g2[2] = {rest, rest + 1}, g3[1] = {rest + 2};
-        epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
-        epi_group<1>(p, e, acc_t, g3, row, col_base, 0);
+        drain_overlapped<C::kOverlapChunks, false>(p, e, acc_t, b, row, col_base,
+                                                   smem_u32(&acc_early[b]));
       } else {
 #pragma unroll
         for (int c = 0; c < C::kChunks; c += 2) {
@@ -503,6 +533,304 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+
+// ---- SM-pair kernel (cta_group::2): 256 x 256 tiles ------------------------------------
+// The two CTAs of a cluster work on one 256 x 256 output tile. Each loads its own 128 rows
+// of A and its own 128 rows of B (so each SM moves half the B bytes of the one-SM kernel)
+// plus the scales for its A rows and for all 256 B rows. The leader (rank 0) issues
+// M=256 x N=256 x K=64 MMAs that read both CTAs' shared memory and write each CTA's TMEM
+// (its 128 rows x 256 columns); both CTAs run scale writers and an epilogue for their own
+// TMEM. Barriers that gather both CTAs live in the leader: the byte counts of both CTAs'
+// A/B loads ("full", TMA with .cta_group::2), the scale slots ("sf_full", 8 arrivals) and the
+// accumulator releases ("acc_empty", "acc_early", 8 arrivals); the leader's commits signal
+// each CTA's own "empty", "sf_empty" and "acc_full" by address.
+struct PairCfg {
+  static constexpr int kABytes = 128 * kBKBytes;       // this CTA's 128 rows of A
+  static constexpr int kBBytes = 128 * kBKBytes;       // this CTA's 128 rows of B
+  static constexpr int kSfaBytes = kKBlocksPerStage * 512;
+  static constexpr int kSfbBytes = 2 * kKBlocksPerStage * 512;  // all 256 rows of B
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 38 KB
+  static constexpr int kStages = 5;
+  static constexpr int kCBufBytes = 32 * 32 * 4;
+  static constexpr int kCBytes = 4 * 2 * kCBufBytes;
+  static constexpr int kBarBytes = 512;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
+  static constexpr int kAccBase1 = kSfCol - 256;       // as in the one-SM N=256 kernel
+  static constexpr int kOverlapChunks = (256 - kAccBase1 + 31) / 32;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_mxf4nvf4_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                              const __grid_constant__ CUtensorMap tmap_b,
+                              const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
+  using C = PairCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + C::kStages * C::kABytes;
+  uint8_t* sSFA = sB + C::kStages * C::kBBytes;
+  uint8_t* sSFB = sSFA + C::kStages * C::kSfaBytes;
+  uint8_t* sC = sSFB + C::kStages * C::kSfbBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
+  uint64_t* full = bars;                    // leader: A/B bytes of both CTAs
+  uint64_t* empty = full + C::kStages;      // each CTA: stage consumed
+  uint64_t* sfd = empty + C::kStages;       // each CTA: its scale bytes landed
+  uint64_t* acc_full = sfd + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;       // leader, 8 arrivals
+  uint64_t* acc_early = acc_full + 4;       // leader, 8 arrivals
+  uint64_t* sf_full = acc_full + 6;         // leader, 8 arrivals
+  uint64_t* sf_empty = sf_full + kSfSlots;
+  uint64_t* drain = sf_empty + kSfSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  auto to_leader = [](const uint64_t* b) { return mapa_shared(smem_u32(b), 0); };
+  auto to_peer = [](const uint64_t* b) { return mapa_shared(smem_u32(b), 1); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+      mbar_init(smem_u32(&sfd[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 8);
+      mbar_init(smem_u32(&acc_early[b]), 8);
+    }
+    for (int j = 0; j < kSfSlots; ++j) {
+      mbar_init(smem_u32(&sf_full[j]), 8);
+      mbar_init(smem_u32(&sf_empty[j]), 1);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    if (p.tma_store) prefetch_tmap(&tmap_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers exist before any cross-CTA arrival or byte count
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both)
+    if (lane == 0) {
+      const uint32_t full_l0 = to_leader(&full[0]);
+      int it = 0;
+      bool ok = true;
+      for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+        int tm, tn;
+        tile_coords(p, t, tm, tn);
+        const int m0 = tm * 256 + static_cast<int>(rank) * 128, n0 = tn * 256;
+        const bool sfa_ok = (m0 / 128) < p.sfa_rowblocks;
+        for (int kt = 0; kt < p.num_kt; ++kt, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+          if (!mbar_wait_cluster(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word,
+                                 kErrWaitSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          int nkb = p.ka - kt * kKBlocksPerStage;
+          if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+          const uint32_t sf_bytes = static_cast<uint32_t>(nkb) * 512u;
+          int nsfb = 0;
+          for (int jb = 0; jb < 2; ++jb)
+            if (n0 / 128 + jb < p.sfb_rowblocks) ++nsfb;
+          if (rank == 0) mbar_arrive_expect_tx(smem_u32(&full[s]), 2 * (C::kABytes + C::kBBytes));
+          const uint32_t fb = full_l0 + s * 8;
+          tma_load_2d_pair(smem_u32(sA + s * C::kABytes), &tmap_a, kt * kBKBytes, m0, fb);
+          tma_load_2d_pair(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes,
+                           n0 + static_cast<int>(rank) * 128, fb);
+          const uint32_t db = smem_u32(&sfd[s]);
+          mbar_arrive_expect_tx(db, sf_bytes * ((sfa_ok ? 1 : 0) + nsfb));
+          if (sfa_ok)
+            bulk_load(smem_u32(sSFA + s * C::kSfaBytes),
+                      p.sfa + (static_cast<size_t>(m0 / 128) * p.ka + kt * kKBlocksPerStage) * 512,
+                      sf_bytes, db);
+          for (int jb = 0; jb < nsfb; ++jb) {
+            const size_t rb = static_cast<size_t>(n0 / 128 + jb);
+            bulk_load(smem_u32(sSFB + s * C::kSfbBytes + jb * kKBlocksPerStage * 512),
+                      p.sfb + (rb * p.ka + kt * kKBlocksPerStage) * 512, sf_bytes, db);
+          }
+        }
+      }
+      if (!ok) {
+        for (int back = 1; back <= C::kStages && it - back >= 0; ++back) {
+          const int f = it - back;
+          mbar_wait_drain(smem_u32(&sfd[f % C::kStages]), static_cast<uint32_t>(f / C::kStages) & 1u,
+                          p.err_word);
+          if (rank == 0)
+            mbar_wait_drain(smem_u32(&full[f % C::kStages]),
+                            static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = make_idesc_mxf4nvf4(256, 256);
+      int it = 0, local = 0;
+      bool ok = true, issued = false;
+      for (int t = cid; t < p.num_tiles && ok; t += ncl, ++local) {
+        const int b = local & 1;
+        const uint32_t u = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait_cluster(smem_u32(&acc_empty[b]), (u & 1u) ^ 1u, abort_flag, p.err_word,
+                               kErrWaitAccEmpty)) {
+          ok = false;
+          break;
+        }
+        if (local > 0) {
+          const uint32_t up = static_cast<uint32_t>((local - 1) >> 1);
+          if (!mbar_wait_cluster(smem_u32(&acc_early[b ^ 1]), up & 1u, abort_flag, p.err_word,
+                                 kErrWaitAccEmpty)) {
+            ok = false;
+            break;
+          }
+        }
+        tc_fence_after();
+        const uint32_t acc_t = tmem_base + (b ? C::kAccBase1 : 0);
+        for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+          if (!mbar_wait_cluster(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word,
+                                 kErrWaitTmaFull)) {
+            ok = false;
+            break;
+          }
+          const int slot = it % kSfSlots;
+          if (!mbar_wait_cluster(smem_u32(&sf_full[slot]), static_cast<uint32_t>(it / kSfSlots) & 1u,
+                                 abort_flag, p.err_word, kErrWaitSfFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          int nkb = p.ka - kt * kKBlocksPerStage;
+          if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+          const uint32_t a_s = smem_u32(sA + s * C::kABytes);
+          const uint32_t b_s = smem_u32(sB + s * C::kBBytes);
+          const uint32_t sf_t = tmem_base + kSfCol + slot * kSfSlotCols;
+          for (int kb = 0; kb < nkb; ++kb) {
+            const uint64_t ad = make_sdesc(a_s + kb * 32, 16, 1024, 2);
+            const uint64_t bd = make_sdesc(b_s + kb * 32, 16, 1024, 2);
+            tc_mma_mxf4nvf4_pair(acc_t, ad, bd, idesc, sf_t + kb * 4, sf_t + kSfbOff + kb * 8,
+                                 (kt > 0 || kb > 0) ? 1u : 0u);
+          }
+          issued = true;
+          tc_commit_pair(smem_u32(&sf_empty[slot]));
+          tc_commit_pair(to_peer(&sf_empty[slot]));
+          tc_commit_pair(smem_u32(&empty[s]));
+          tc_commit_pair(to_peer(&empty[s]));
+        }
+        if (!ok) break;
+        tc_commit_pair(smem_u32(&acc_full[b]));
+        tc_commit_pair(to_peer(&acc_full[b]));
+      }
+      if (!ok && issued) {
+        tc_commit_pair(smem_u32(drain));
+        mbar_wait_drain(smem_u32(drain), 0, p.err_word);
+      }
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------ scale writers (both)
+    const int q = warp & 3;
+    const int wgroup = (warp - 6) >> 2;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t sf_full_l0 = to_leader(&sf_full[0]);
+    int it = 0;
+    bool ok = true;
+    for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+      for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
+        if ((it % kWriterGroups) != wgroup) continue;
+        const int s = it % C::kStages;
+        const int slot = it % kSfSlots;
+        if (!mbar_wait(smem_u32(&sfd[s]), static_cast<uint32_t>(it / C::kStages) & 1u, abort_flag,
+                       p.err_word, kErrWaitTmaFull)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* sfa_s = sSFA + s * C::kSfaBytes + lane * 16;
+        const uint8_t* sfb_s = sSFB + s * C::kSfbBytes + lane * 16;
+        uint32_t va[16], vb[32];
+#pragma unroll
+        for (int kb = 0; kb < kKBlocksPerStage; ++kb) {
+          const uint4 w = *reinterpret_cast<const uint4*>(sfa_s + kb * 512);
+          va[4 * kb + 0] = w.x; va[4 * kb + 1] = w.y; va[4 * kb + 2] = w.z; va[4 * kb + 3] = w.w;
+#pragma unroll
+          for (int jb = 0; jb < 2; ++jb) {
+            const uint4 x = *reinterpret_cast<const uint4*>(sfb_s + jb * kKBlocksPerStage * 512 + kb * 512);
+            const int o = kb * 8 + 4 * jb;
+            vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
+          }
+        }
+        if (!mbar_wait_cluster(smem_u32(&sf_empty[slot]),
+                               (static_cast<uint32_t>(it / kSfSlots) & 1u) ^ 1u, abort_flag,
+                               p.err_word, kErrWaitSfEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sf_t = lane_base + kSfCol + slot * kSfSlotCols;
+        tmem_st_32x32b_x16(sf_t, va);
+        tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
+        tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(sf_full_l0 + slot * 8);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both)
+    const int q = warp & 3;
+    const int row_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
+    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0};
+    const uint32_t early_l0 = to_leader(&acc_early[0]);
+    const uint32_t empty_l0 = to_leader(&acc_empty[0]);
+    int local = 0;
+    for (int t = cid; t < p.num_tiles; t += ncl, ++local) {
+      const int b = local & 1;
+      const uint32_t u = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait_cluster(smem_u32(&acc_full[b]), u & 1u, abort_flag, p.err_word,
+                             kErrWaitAccFull))
+        break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      const int row = tm * 256 + row_in_tile;
+      const int col_base = tn * 256;
+      e.row0 = tm * 256 + static_cast<int>(rank) * 128 + q * 32;
+      const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             (b ? C::kAccBase1 : 0);
+      drain_overlapped<C::kOverlapChunks, true>(p, e, acc_t, b, row, col_base, early_l0 + b * 8);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(empty_l0 + b * 8);
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into the peer's TMEM are complete on both sides
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
 // One CTA waits on an mbarrier nothing completes, with a short limit: exercises the
@@ -594,6 +922,8 @@ struct DeviceState {
   int sms = 0;
   int cc_major = 0, cc_minor = 0;
   bool attr_set[2] = {false, false};
+  bool pair_attr_set = false;
+  int pair_clusters = 0;  // co-resident SM-pair clusters of the pair kernel
   uint32_t* err_word = nullptr;
   // Workspace for canonical -> tcgen05 scale reordering (grown on demand).
   uint8_t* ws = nullptr;
@@ -653,6 +983,44 @@ bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_err(err, std::string("gemm launch: ") + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+bool launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                 const GemmParams& p, DeviceState* ds, cudaStream_t s, std::string* err) {
+  using C = PairCfg;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!ds->pair_attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_mxf4nvf4_pair_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) {
+      set_err(err, std::string("cudaFuncSetAttribute (pair): ") + cudaGetErrorString(e));
+      return false;
+    }
+    int ncl = 0;
+    cfg.gridDim = dim3(2 * (ds->sms / 2), 1, 1);
+    e = cudaOccupancyMaxActiveClusters(&ncl, gemm_mxf4nvf4_pair_kernel, &cfg);
+    if (e != cudaSuccess || ncl < 1) ncl = ds->sms / 2;
+    ds->pair_clusters = ncl;
+    ds->pair_attr_set = true;
+  }
+  const int ncl = p.num_tiles < ds->pair_clusters ? p.num_tiles : ds->pair_clusters;
+  cfg.gridDim = dim3(2 * ncl, 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_mxf4nvf4_pair_kernel, ta, tb, tc, p);
+  if (e != cudaSuccess) {
+    set_err(err, std::string("gemm (pair) launch: ") + cudaGetErrorString(e));
     return false;
   }
   return true;
@@ -737,6 +1105,22 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   if (!ds) return false;
   int bn = op.tile_n;
   const int tiles_m = (op.M + kBM - 1) / kBM;
+  // SM pairs (256 x 256 tiles) whenever there are enough of those tiles to fill the GPU's
+  // pairs once; one-SM tiles for small problems.
+  int cg = op.cta_group;
+  const long pair_tiles = static_cast<long>((op.M + 255) / 256) * ((op.N + 255) / 256);
+  if (cg == 0) cg = (op.M > 128 && pair_tiles >= ds->sms / 2 && (bn == 0 || bn == 256)) ? 2 : 1;
+  if (cg != 1 && cg != 2) {
+    set_err(err, "cta_group must be 0, 1 or 2");
+    return false;
+  }
+  if (cg == 2) {
+    if (bn != 0 && bn != 256) {
+      set_err(err, "SM-pair tiles are 256 x 256 (tile_n must be 0 or 256 with cta_group 2)");
+      return false;
+    }
+    bn = 256;
+  }
   if (bn == 0) bn = (static_cast<long>(tiles_m) * ((op.N + 255) / 256) >= ds->sms) ? 256 : 128;
   if (bn != 128 && bn != 256) {
     set_err(err, "tile_n must be 128 or 256 for the dense kernel");
@@ -752,17 +1136,19 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   p.ldc = op.N;
   p.alpha = op.a_global * op.b_global;
   p.out_bf16 = (op.d != nullptr && op.out_dtype == OutDType::BF16) ? 1 : 0;
-  p.tiles_m = tiles_m;
+  p.tiles_m = cg == 2 ? (op.M + 255) / 256 : tiles_m;
   p.tiles_n = (op.N + bn - 1) / bn;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.group_m = 16;
   p.ka = (op.K + 63) / 64;
   p.num_kt = (op.K + 255) / 256;
   p.sfb_rowblocks = (op.N + 127) / 128;
+  p.sfa_rowblocks = (op.M + 127) / 128;
+  p.group_m = cg == 2 ? 8 : 16;
   p.err_word = ds->err_word;
   CUtensorMap ta, tb;
   if (!encode_operand_map(&ta, op.a_packed, op.M, op.K, kBM, err)) return false;
-  if (!encode_operand_map(&tb, op.b_packed, op.N, op.K, bn, err)) return false;
+  if (!encode_operand_map(&tb, op.b_packed, op.N, op.K, cg == 2 ? 128 : bn, err)) return false;
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   const int esize = p.out_bf16 ? 2 : 4;
@@ -770,6 +1156,7 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
                  (reinterpret_cast<uintptr_t>(out) & 15) == 0)
                     ? 1 : 0;
   if (p.tma_store && !encode_output_map(&tc, out, op.M, op.N, p.out_bf16 != 0, err)) return false;
+  if (cg == 2) return launch_pair(ta, tb, tc, p, ds, s, err);
   return bn == 256 ? launch_dense<256>(ta, tb, tc, p, ds, s, err)
                    : launch_dense<128>(ta, tb, tc, p, ds, s, err);
 }

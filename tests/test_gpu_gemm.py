@@ -97,3 +97,22 @@ def test_rejects_bad_k(api):
     with pytest.raises(api.Nvfp4Error):
         api.gemm(t.packed, t.scales, t.packed, t.scales, 128, 128, 48, out,
                  sf_layout=api.SF_CANONICAL)
+
+
+@pytest.mark.parametrize("shape", [(256, 256, 256), (512, 768, 1024), (300, 520, 288), (100, 256, 64),
+                                   (1000, 1000, 2048), (2048, 4096, 512)])
+@pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
+def test_sm_pair_kernel(api, orc, shape, out):
+    """The cta_group::2 kernel (256 x 256 tiles on SM pairs), forced, on ragged shapes."""
+    M, N, K = shape
+    _case(api, orc, M, N, K, seed=M * 7 + N + K, out=out, cta_group=2)
+
+
+def test_sm_pair_matches_one_sm(api):
+    """Both kernels accumulate in FP32 per K-block in the same order: identical outputs."""
+    M, N, K = 1024, 2048, 1024
+    _, a = make_operand(api, M, K, 21)
+    _, b = make_operand(api, N, K, 22)
+    c1 = run_gemm(api, a, b, M, N, K, cta_group=1, tile_n=256)
+    c2 = run_gemm(api, a, b, M, N, K, cta_group=2)
+    assert torch.equal(c1, c2)
