@@ -65,10 +65,8 @@ constexpr int kKBlocksPerStage = 4;  // MMA K = 64 -> 4 MMAs per stage
 constexpr int kNumThreads = 448;  // 14 warps
 constexpr int kWriterGroups = 2;  // scale writers: two warps per TMEM quadrant, even/odd stages
 constexpr int kTmemCols = 512;
-constexpr int kSfSlots = 3;       // ring of per-stage scale slots in TMEM
-constexpr int kSfSlotCols = 48;   // SFA at +4*kb (16 columns), SFB at +16 + 8*kb (32 columns)
+constexpr int kSfSlotCols = 48;   // per stage: SFA at +4*kb (16 columns), SFB at +16 + 8*kb
 constexpr int kSfbOff = 16;
-constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368
 
 template <int BN>
 struct Cfg {
@@ -82,7 +80,10 @@ struct Cfg {
   static constexpr int kCBytes = 4 * 2 * kCBufBytes;            // 4 warps, double-buffered
   static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
-  // TMEM: accumulator buffers and which 32-column chunks are shared between them.
+  // TMEM: one scale slot per smem stage (so a stage's "empty" also frees its slot) at the top,
+  // two accumulator buffers below; which 32-column chunks the buffers share.
+  static constexpr int kSfSlots = kStages;
+  static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368 / 272
   static constexpr int kAccBase1 = (BN == 256) ? kSfCol - 256 : BN;  // 112 for BN = 256
   static constexpr int kChunks = BN / 32;
   static constexpr bool kOverlap = (BN == 256);
@@ -91,7 +92,7 @@ struct Cfg {
   static constexpr int kSfbAtoms = (BN + 127) / 128;
   static constexpr int kSfbColsPerKb = kSfbAtoms * 4;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static_assert(kAccBase1 + BN <= kSfCol, "TMEM budget");
+  static_assert(kAccBase1 + BN <= kSfCol && kAccBase1 >= 0, "TMEM budget");
   static_assert(!kOverlap || (kOverlapChunks >= 4 && kOverlapChunks <= 6), "overlap chunks");
 };
 
@@ -286,14 +287,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint8_t* sSFB = sSFA + C::kStages * C::kSfaBytes;
   uint8_t* sC = sSFB + C::kStages * C::kSfbBytes;  // 1024-aligned: stages are multiples of 1 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + C::kStages;
-  uint64_t* acc_full = bars + 2 * C::kStages;
+  uint64_t* full = bars;                // A/B bytes + producer + the stage's 4 scale writers
+  uint64_t* empty = bars + C::kStages;  // stage (smem and its TMEM scale slot) consumed
+  uint64_t* sfd = empty + C::kStages;   // the stage's scale bytes landed in smem
+  uint64_t* acc_full = sfd + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* acc_early = acc_full + 4;
-  uint64_t* sf_full = acc_full + 6;
-  uint64_t* sf_empty = sf_full + kSfSlots;
-  uint64_t* drain = sf_empty + kSfSlots;
+  uint64_t* drain = acc_full + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -302,17 +302,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&full[s]), 1 + 4);
       mbar_init(smem_u32(&empty[s]), 1);
+      mbar_init(smem_u32(&sfd[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&acc_empty[b]), 4);
       mbar_init(smem_u32(&acc_early[b]), 4);
-    }
-    for (int j = 0; j < kSfSlots; ++j) {
-      mbar_init(smem_u32(&sf_full[j]), 4);
-      mbar_init(smem_u32(&sf_empty[j]), 1);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -353,25 +350,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           int nsfb = 0;
           for (int jb = 0; jb < (BN + 127) / 128; ++jb)
             if (n0 / 128 + jb < p.sfb_rowblocks) ++nsfb;
-          const uint32_t fb = smem_u32(&full[s]);
-          mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes + sf_bytes * (1 + nsfb));
-          tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * kBKBytes, m0, fb);
-          tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes, n0, fb);
+          const uint32_t db = smem_u32(&sfd[s]);
+          mbar_arrive_expect_tx(db, sf_bytes * (1 + nsfb));
           bulk_load(smem_u32(sSFA + s * C::kSfaBytes),
                     p.sfa + (static_cast<size_t>(tm) * p.ka + kt * kKBlocksPerStage) * 512,
-                    sf_bytes, fb);
+                    sf_bytes, db);
           for (int jb = 0; jb < nsfb; ++jb) {
             const size_t rb = static_cast<size_t>(n0 / 128 + jb);
             bulk_load(smem_u32(sSFB + s * C::kSfbBytes + jb * kKBlocksPerStage * 512),
-                      p.sfb + (rb * p.ka + kt * kKBlocksPerStage) * 512, sf_bytes, fb);
+                      p.sfb + (rb * p.ka + kt * kKBlocksPerStage) * 512, sf_bytes, db);
           }
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes);
+          tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * kBKBytes, m0, fb);
+          tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes, n0, fb);
         }
       }
       if (!ok) {
         // Drain: the most recent fill of every stage must land before the CTA exits.
         for (int back = 1; back <= C::kStages && it - back >= 0; ++back) {
           const int f = it - back;
-          mbar_wait_drain(smem_u32(&full[f % C::kStages]),
+          mbar_wait_drain(smem_u32(&sfd[f % C::kStages]),
                           static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
         }
       }
@@ -405,30 +404,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
           const int s = it % C::kStages;
           const uint32_t j = static_cast<uint32_t>(it / C::kStages);
-          if (!mbar_wait(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word, kErrWaitTmaFull)) {
-            ok = false;
-            break;
-          }
-          const int slot = it % kSfSlots;
-          if (!mbar_wait(smem_u32(&sf_full[slot]), static_cast<uint32_t>(it / kSfSlots) & 1u,
-                         abort_flag, p.err_word, kErrWaitSfFull)) {
+          // One spin-wait per stage: A/B bytes, producer and the stage's scale writers.
+          if (!mbar_spin_wait<false>(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word,
+                                     kErrWaitTmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
           int nkb = p.ka - kt * kKBlocksPerStage;
           if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
-          const uint32_t a_s = smem_u32(sA + s * C::kABytes);
-          const uint32_t b_s = smem_u32(sB + s * C::kBBytes);
-          const uint32_t sf_t = tmem_base + kSfCol + slot * kSfSlotCols;
-          for (int kb = 0; kb < nkb; ++kb) {
-            const uint64_t ad = make_sdesc(a_s + kb * 32, 16, 1024, 2);
-            const uint64_t bd = make_sdesc(b_s + kb * 32, 16, 1024, 2);
-            tc_mma_mxf4nvf4(acc_t, ad, bd, idesc, sf_t + kb * 4,
-                            sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
+          // Descriptor start addresses are in 16-byte units: +2 per 32-byte K-block.
+          const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 1024, 2);
+          const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
+          const uint32_t sf_t = tmem_base + C::kSfCol + s * kSfSlotCols;
+          if (nkb == kKBlocksPerStage) {
+#pragma unroll
+            for (int kb = 0; kb < kKBlocksPerStage; ++kb)
+              tc_mma_mxf4nvf4(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
+                              sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
+          } else {
+            for (int kb = 0; kb < nkb; ++kb)
+              tc_mma_mxf4nvf4(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
+                              sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
           }
           issued = true;
-          tc_commit(smem_u32(&sf_empty[slot]));
           tc_commit(smem_u32(&empty[s]));
         }
         if (!ok) break;
@@ -452,10 +451,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
       for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
         if ((it % kWriterGroups) != wgroup) continue;
-        const int s = it % C::kStages;
-        const int slot = it % kSfSlots;
-        if (!mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>(it / C::kStages) & 1u, abort_flag,
-                       p.err_word, kErrWaitTmaFull)) {
+        const int s = it % C::kStages;  // also the TMEM scale slot
+        const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+        if (!mbar_wait(smem_u32(&sfd[s]), j & 1u, abort_flag, p.err_word, kErrWaitTmaFull)) {
           ok = false;
           break;
         }
@@ -474,20 +472,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
           }
         }
-        if (!mbar_wait(smem_u32(&sf_empty[slot]), (static_cast<uint32_t>(it / kSfSlots) & 1u) ^ 1u,
-                       abort_flag, p.err_word, kErrWaitSfEmpty)) {
+        // The slot is free once the MMAs of the stage that last used it completed.
+        if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word, kErrWaitSfEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sf_t = lane_base + kSfCol + slot * kSfSlotCols;
+        const uint32_t sf_t = lane_base + C::kSfCol + s * kSfSlotCols;
         tmem_st_32x32b_x16(sf_t, va);
         tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
         if (C::kSfbAtoms == 2) tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&sf_full[slot]));
+        if (lane == 0) mbar_arrive(smem_u32(&full[s]));
       }
     }
   } else {
@@ -557,7 +555,9 @@ struct PairCfg {
   static constexpr int kCBytes = 4 * 2 * kCBufBytes;
   static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
-  static constexpr int kAccBase1 = kSfCol - 256;       // as in the one-SM N=256 kernel
+  static constexpr int kSfSlots = 3;                    // ring of per-stage scale slots
+  static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368
+  static constexpr int kAccBase1 = kSfCol - 256;       // 112, as in the one-SM N=256 kernel
   static constexpr int kOverlapChunks = (256 - kAccBase1 + 31) / 32;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -582,9 +582,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* acc_full = sfd + C::kStages;
   uint64_t* acc_empty = acc_full + 2;       // leader, 8 arrivals
   uint64_t* acc_early = acc_full + 4;       // leader, 8 arrivals
-  uint64_t* sf_full = acc_full + 6;         // leader, 8 arrivals
-  uint64_t* sf_empty = sf_full + kSfSlots;
-  uint64_t* drain = sf_empty + kSfSlots;
+  uint64_t* sf_empty = acc_full + 6;        // each CTA: scale slot consumed
+  uint64_t* drain = sf_empty + C::kSfSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -597,7 +596,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&full[s]), 1 + 8);  // leader's expect_tx + both CTAs' scale writers
       mbar_init(smem_u32(&empty[s]), 1);
       mbar_init(smem_u32(&sfd[s]), 1);
     }
@@ -606,10 +605,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&acc_empty[b]), 8);
       mbar_init(smem_u32(&acc_early[b]), 8);
     }
-    for (int j = 0; j < kSfSlots; ++j) {
-      mbar_init(smem_u32(&sf_full[j]), 8);
-      mbar_init(smem_u32(&sf_empty[j]), 1);
-    }
+    for (int j = 0; j < C::kSfSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -708,28 +704,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
           const int s = it % C::kStages;
           const uint32_t j = static_cast<uint32_t>(it / C::kStages);
-          if (!mbar_wait_cluster(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word,
-                                 kErrWaitTmaFull)) {
+          // One spin-wait per stage: both CTAs' A/B bytes and both CTAs' scale writers.
+          if (!mbar_spin_wait<true>(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word,
+                                    kErrWaitTmaFull)) {
             ok = false;
             break;
           }
-          const int slot = it % kSfSlots;
-          if (!mbar_wait_cluster(smem_u32(&sf_full[slot]), static_cast<uint32_t>(it / kSfSlots) & 1u,
-                                 abort_flag, p.err_word, kErrWaitSfFull)) {
-            ok = false;
-            break;
-          }
+          const int slot = it % C::kSfSlots;
           tc_fence_after();
           int nkb = p.ka - kt * kKBlocksPerStage;
           if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
-          const uint32_t a_s = smem_u32(sA + s * C::kABytes);
-          const uint32_t b_s = smem_u32(sB + s * C::kBBytes);
-          const uint32_t sf_t = tmem_base + kSfCol + slot * kSfSlotCols;
-          for (int kb = 0; kb < nkb; ++kb) {
-            const uint64_t ad = make_sdesc(a_s + kb * 32, 16, 1024, 2);
-            const uint64_t bd = make_sdesc(b_s + kb * 32, 16, 1024, 2);
-            tc_mma_mxf4nvf4_pair(acc_t, ad, bd, idesc, sf_t + kb * 4, sf_t + kSfbOff + kb * 8,
-                                 (kt > 0 || kb > 0) ? 1u : 0u);
+          const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 1024, 2);
+          const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
+          const uint32_t sf_t = tmem_base + C::kSfCol + slot * kSfSlotCols;
+          if (nkb == kKBlocksPerStage) {
+#pragma unroll
+            for (int kb = 0; kb < kKBlocksPerStage; ++kb)
+              tc_mma_mxf4nvf4_pair(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
+                                   sf_t + kSfbOff + kb * 8, (kt > 0 || kb > 0) ? 1u : 0u);
+          } else {
+            for (int kb = 0; kb < nkb; ++kb)
+              tc_mma_mxf4nvf4_pair(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
+                                   sf_t + kSfbOff + kb * 8, (kt > 0 || kb > 0) ? 1u : 0u);
           }
           issued = true;
           tc_commit_pair(smem_u32(&sf_empty[slot]));
@@ -751,14 +747,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int q = warp & 3;
     const int wgroup = (warp - 6) >> 2;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t sf_full_l0 = to_leader(&sf_full[0]);
+    const uint32_t full_l0 = to_leader(&full[0]);
     int it = 0;
     bool ok = true;
     for (int t = cid; t < p.num_tiles && ok; t += ncl) {
       for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
         if ((it % kWriterGroups) != wgroup) continue;
         const int s = it % C::kStages;
-        const int slot = it % kSfSlots;
+        const int slot = it % C::kSfSlots;
         if (!mbar_wait(smem_u32(&sfd[s]), static_cast<uint32_t>(it / C::kStages) & 1u, abort_flag,
                        p.err_word, kErrWaitTmaFull)) {
           ok = false;
@@ -779,20 +775,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
         if (!mbar_wait_cluster(smem_u32(&sf_empty[slot]),
-                               (static_cast<uint32_t>(it / kSfSlots) & 1u) ^ 1u, abort_flag,
+                               (static_cast<uint32_t>(it / C::kSfSlots) & 1u) ^ 1u, abort_flag,
                                p.err_word, kErrWaitSfEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sf_t = lane_base + kSfCol + slot * kSfSlotCols;
+        const uint32_t sf_t = lane_base + C::kSfCol + slot * kSfSlotCols;
         tmem_st_32x32b_x16(sf_t, va);
         tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
         tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(sf_full_l0 + slot * 8);
+        if (lane == 0) mbar_arrive_cluster(full_l0 + s * 8);
       }
     }
   } else {
