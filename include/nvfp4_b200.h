@@ -54,6 +54,22 @@ typedef struct Nvfp4GemmArgs {
  * NVFP4_SF_CANONICAL the call reorders the scales into a per-device workspace first. */
 int nvfp4_b200_gemm(const Nvfp4GemmArgs* args, void* stream, char* err, size_t errlen);
 
+/* No counterpart in the reference. Same GEMM as nvfp4_b200_gemm with canonical scales
+ * (dense mode, sf_layout must be NVFP4_SF_CANONICAL) for callers that cannot let the library
+ * allocate device memory: code inside CUDA-graph capture, servers that pre-partition all GPU
+ * memory into their own pool, latency-critical loops that cannot afford cudaMalloc's implicit
+ * synchronisation. The scale reorder goes into a fixed 16 MiB scratch array compiled into the
+ * library (held on every GPU that loads it until exit) instead of a cudaMalloc'd workspace;
+ * problems whose reordered scales exceed it ((M+N)*K/16 bytes, roughly) are rejected with
+ * NVFP4_B200_EINVAL. The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current): make it before any stream capture.
+ * Calls share the array: calls on the same device whose work overlaps on the GPU race. */
+int nvfp4_b200_gemm_noalloc(const Nvfp4GemmArgs* args, void* stream, char* err, size_t errlen);
+
+/* Size in bytes of the scratch array nvfp4_b200_gemm_noalloc reorders scales into. No
+ * counterpart in the reference. */
+size_t nvfp4_b200_gemm_noalloc_scratch_bytes(void);
+
 /* Replaces quantize_to_nvfp4 - src/nvfp4.h:40-42, src/nvfp4.cu:62-97 - on the GPU,
  * byte-identical to it. src: fp32 [rows][cols] (cols % 16 == 0). Writes packed
  * [rows][cols/2], and the scales in the canonical layout (scales, may be NULL) and/or the

@@ -29,6 +29,7 @@ EXPORTED = [
     "nvfp4_b200_fill_uniform", "nvfp4_b200_fill_normal", "nvfp4_b200_sf_tcgen05_bytes",
     "nvfp4_b200_sf_to_tcgen05", "nvfp4_b200_measure_bandwidth", "nvfp4_b200_peak",
     "nvfp4_b200_device_error", "nvfp4_b200_wait_selftest", "nvfp4_b200_version",
+    "nvfp4_b200_gemm_noalloc", "nvfp4_b200_gemm_noalloc_scratch_bytes",
 ]
 
 
@@ -66,6 +67,9 @@ def lib():
         vp, sz, ip = C.c_void_p, C.c_size_t, C.c_int
         errs = [C.c_char_p, sz]
         L.nvfp4_b200_gemm.argtypes = [C.POINTER(GemmArgs), vp, *errs]
+        L.nvfp4_b200_gemm_noalloc.argtypes = [C.POINTER(GemmArgs), vp, *errs]
+        L.nvfp4_b200_gemm_noalloc_scratch_bytes.argtypes = []
+        L.nvfp4_b200_gemm_noalloc_scratch_bytes.restype = sz
         L.nvfp4_b200_quantize.argtypes = [vp, ip, ip, C.c_float, vp, vp, vp, vp, *errs]
         L.nvfp4_b200_dequantize.argtypes = [vp, vp, ip, ip, C.c_float, vp, vp, *errs]
         L.nvfp4_b200_fill_uniform.argtypes = [vp, ip, ip, C.c_uint64, vp, *errs]
@@ -80,7 +84,8 @@ def lib():
         L.nvfp4_b200_wait_selftest.argtypes = [C.c_uint64, C.POINTER(C.c_uint32), *errs]
         L.nvfp4_b200_version.restype = C.c_char_p
         for name in EXPORTED:
-            if name not in ("nvfp4_b200_sf_tcgen05_bytes", "nvfp4_b200_version"):
+            if name not in ("nvfp4_b200_sf_tcgen05_bytes", "nvfp4_b200_version",
+                            "nvfp4_b200_gemm_noalloc_scratch_bytes"):
                 getattr(L, name).restype = C.c_int
         _lib = L
     return _lib

@@ -87,6 +87,38 @@ int nvfp4_b200_gemm(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errl
   return ok(err, errlen);
 }
 
+int nvfp4_b200_gemm_noalloc(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errlen) {
+  if (!a) return fail(NVFP4_B200_EINVAL, "null args", err, errlen);
+  if (a->mode != NVFP4_MODE_DENSE)
+    return fail(NVFP4_B200_EINVAL, "the no-alloc GEMM supports dense mode only", err, errlen);
+  if (a->sf_layout != NVFP4_SF_CANONICAL)
+    return fail(NVFP4_B200_EINVAL, "the no-alloc GEMM takes canonical scales", err, errlen);
+  if (a->out_dtype != NVFP4_OUT_F32 && a->out_dtype != NVFP4_OUT_BF16)
+    return fail(NVFP4_B200_EINVAL, "unknown out_dtype", err, errlen);
+  Nvfp4DeviceOperands op;
+  op.a_packed = static_cast<const uint8_t*>(a->a_packed);
+  op.a_scales = static_cast<const uint8_t*>(a->a_scales);
+  op.a_global = a->a_global;
+  op.b_packed = static_cast<const uint8_t*>(a->b_packed);
+  op.b_scales = static_cast<const uint8_t*>(a->b_scales);
+  op.b_global = a->b_global;
+  op.M = a->M;
+  op.N = a->N;
+  op.K = a->K;
+  op.mode = GemmMode::Dense;
+  op.sf_layout = SfLayout::Canonical;
+  op.out_dtype = a->out_dtype == NVFP4_OUT_BF16 ? OutDType::BF16 : OutDType::F32;
+  op.d = a->c;
+  op.cta_group = a->cta_group;
+  op.tile_n = a->tile_n;
+  std::string e;
+  if (!nvfp4b200::gemm_noalloc(op, static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+size_t nvfp4_b200_gemm_noalloc_scratch_bytes(void) { return nvfp4b200::noalloc_scratch_bytes(); }
+
 int nvfp4_b200_quantize(const float* src, int rows, int cols, float global_scale, void* packed,
                         void* scales, void* scales_tc, void* stream, char* err, size_t errlen) {
   std::string e;

@@ -20,6 +20,9 @@ bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err)
 // Dense GEMM with scales already in the tcgen05 layout; `out` is op.d or op.c.
 bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb,
                    void* out, cudaStream_t s, std::string* err);
+// Canonical-scale dense GEMM that reorders into a fixed static scratch (gemm_noalloc.cu).
+bool gemm_noalloc(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
+size_t noalloc_scratch_bytes();
 bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
 uint32_t* device_error_word(std::string* err);
 bool wait_selftest(uint64_t limit_ns, std::string* err);

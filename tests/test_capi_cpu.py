@@ -33,7 +33,7 @@ def declared_symbols():
 def test_exports_every_declared_symbol(lib):
     decl = declared_symbols()
     assert decl, "no C-ABI declarations found"
-    assert decl == set(api.EXPORTED)
+    assert decl == set(api.EXPORTED), decl ^ set(api.EXPORTED)
     for name in decl:
         assert hasattr(lib, name), name
 
