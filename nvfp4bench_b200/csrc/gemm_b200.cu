@@ -540,8 +540,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 // plus the scales for its A rows and for all 256 B rows. The leader (rank 0) issues
 // M=256 x N=256 x K=64 MMAs that read both CTAs' shared memory and write each CTA's TMEM
 // (its 128 rows x 256 columns); both CTAs run scale writers and an epilogue for their own
-// TMEM. Barriers that gather both CTAs live in the leader: the byte counts of both CTAs'
-// A/B loads ("full", TMA with .cta_group::2), the scale slots ("sf_full", 8 arrivals) and the
+// TMEM. Barriers that gather both CTAs live in the leader: "full" (both CTAs' A/B byte
+// counts through TMA with .cta_group::2 plus both CTAs' scale writers, 1 + 8 arrivals) and the
 // accumulator releases ("acc_empty", "acc_early", 8 arrivals); the leader's commits signal
 // each CTA's own "empty", "sf_empty" and "acc_full" by address.
 struct PairCfg {
@@ -913,6 +913,50 @@ bool encode_output_map(CUtensorMap* map, void* base, int M, int N, bool bf16, st
   return true;
 }
 
+// Small cache of encoded tensor maps: encoding is pure host work (a few microseconds per map)
+// that would otherwise sit in front of every launch. A map depends only on the key below, so
+// a hit is exact; entries are replaced round-robin.
+struct MapKey {
+  const void* base;
+  long rows, cols;
+  int box, kind;  // kind: 0 = operand, 1 = BF16 output, 2 = FP32 output
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && box == o.box && kind == o.kind;
+  }
+};
+struct MapCache {
+  static constexpr int kEntries = 64;
+  MapKey key[kEntries];
+  CUtensorMap map[kEntries];
+  bool used[kEntries] = {};
+  int next = 0;
+  std::mutex mu;
+};
+MapCache g_maps;
+
+bool cached_map(const MapKey& k, CUtensorMap* out, std::string* err) {
+  {
+    std::lock_guard<std::mutex> lk(g_maps.mu);
+    for (int i = 0; i < MapCache::kEntries; ++i)
+      if (g_maps.used[i] && g_maps.key[i] == k) {
+        *out = g_maps.map[i];
+        return true;
+      }
+  }
+  bool ok = k.kind == 0 ? encode_operand_map(out, k.base, static_cast<int>(k.rows),
+                                             static_cast<int>(k.cols), k.box, err)
+                        : encode_output_map(out, const_cast<void*>(k.base), static_cast<int>(k.rows),
+                                            static_cast<int>(k.cols), k.kind == 1, err);
+  if (!ok) return false;
+  std::lock_guard<std::mutex> lk(g_maps.mu);
+  const int i = g_maps.next;
+  g_maps.next = (i + 1) % MapCache::kEntries;
+  g_maps.key[i] = k;
+  g_maps.map[i] = *out;
+  g_maps.used[i] = true;
+  return true;
+}
+
 struct DeviceState {
   bool init = false;
   int sms = 0;
@@ -1101,11 +1145,10 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   if (!ds) return false;
   int bn = op.tile_n;
   const int tiles_m = (op.M + kBM - 1) / kBM;
-  // SM pairs (256 x 256 tiles) whenever there are enough of those tiles to fill the GPU's
-  // pairs once; one-SM tiles for small problems.
+  // Default: one-SM tiles (measured faster than the SM-pair kernel on B200 so far); the
+  // SM-pair kernel (256 x 256 tiles) on request.
   int cg = op.cta_group;
-  const long pair_tiles = static_cast<long>((op.M + 255) / 256) * ((op.N + 255) / 256);
-  if (cg == 0) cg = (op.M > 128 && pair_tiles >= ds->sms / 2 && (bn == 0 || bn == 256)) ? 2 : 1;
+  if (cg == 0) cg = 1;
   if (cg != 1 && cg != 2) {
     set_err(err, "cta_group must be 0, 1 or 2");
     return false;
@@ -1143,15 +1186,17 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   p.group_m = cg == 2 ? 8 : 16;
   p.err_word = ds->err_word;
   CUtensorMap ta, tb;
-  if (!encode_operand_map(&ta, op.a_packed, op.M, op.K, kBM, err)) return false;
-  if (!encode_operand_map(&tb, op.b_packed, op.N, op.K, cg == 2 ? 128 : bn, err)) return false;
+  if (!cached_map(MapKey{op.a_packed, op.M, op.K, kBM, 0}, &ta, err)) return false;
+  if (!cached_map(MapKey{op.b_packed, op.N, op.K, cg == 2 ? 128 : bn, 0}, &tb, err)) return false;
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   const int esize = p.out_bf16 ? 2 : 4;
   p.tma_store = ((static_cast<size_t>(op.N) * esize) % 16 == 0 &&
                  (reinterpret_cast<uintptr_t>(out) & 15) == 0)
                     ? 1 : 0;
-  if (p.tma_store && !encode_output_map(&tc, out, op.M, op.N, p.out_bf16 != 0, err)) return false;
+  if (p.tma_store &&
+      !cached_map(MapKey{out, op.M, op.N, 32, p.out_bf16 ? 1 : 2}, &tc, err))
+    return false;
   if (cg == 2) return launch_pair(ta, tb, tc, p, ds, s, err);
   return bn == 256 ? launch_dense<256>(ta, tb, tc, p, ds, s, err)
                    : launch_dense<128>(ta, tb, tc, p, ds, s, err);
