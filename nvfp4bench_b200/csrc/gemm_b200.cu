@@ -1143,6 +1143,12 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
                    void* out, cudaStream_t s, std::string* err) {
   DeviceState* ds = device_state(err);
   if (!ds) return false;
+  // Few tokens and few 128-row weight tiles (e.g. M=16 x a 4096-row weight): the split-K
+  // weight-streaming kernel keeps every SM loading; measured slower than the general kernel
+  // once the weight alone has enough tiles to occupy half the SMs. An explicit tile shape or
+  // SM grouping selects the general kernel.
+  if (op.M <= 32 && (op.N + 127) / 128 < ds->sms / 2 && op.cta_group == 0 && op.tile_n == 0)
+    return gemm_decode(op, sfa, sfb, out, s, err);
   int bn = op.tile_n;
   const int tiles_m = (op.M + kBM - 1) / kBM;
   // Default: one-SM tiles (measured faster than the SM-pair kernel on B200 so far); the
@@ -1200,6 +1206,16 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   if (cg == 2) return launch_pair(ta, tb, tc, p, ds, s, err);
   return bn == 256 ? launch_dense<256>(ta, tb, tc, p, ds, s, err)
                    : launch_dense<128>(ta, tb, tc, p, ds, s, err);
+}
+
+bool operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows,
+                 std::string* err) {
+  return cached_map(MapKey{base, rows, K, box_rows, 0}, map, err);
+}
+
+int device_sms(std::string* err) {
+  DeviceState* ds = device_state(err);
+  return ds ? ds->sms : 0;
 }
 
 bool wait_selftest(uint64_t limit_ns, std::string* err) {

@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <string>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "gemm.h"
@@ -25,6 +26,14 @@ bool gemm_noalloc(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* er
 size_t noalloc_scratch_bytes();
 bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
 uint32_t* device_error_word(std::string* err);
+// Tensor map of a packed FP4 operand [rows][K/2] (box 128 bytes x box_rows, 128-byte
+// swizzle), from the engine's map cache.
+bool operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows,
+                 std::string* err);
+int device_sms(std::string* err);
+// Weight-streaming GEMM for M <= 128 tokens (gemm_decode.cu); scales in the tcgen05 layout.
+bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb,
+                 void* out, cudaStream_t s, std::string* err);
 bool wait_selftest(uint64_t limit_ns, std::string* err);
 
 // ---- codecs (codec.cu) ---------------------------------------------------------------

@@ -116,3 +116,38 @@ def test_sm_pair_matches_one_sm(api):
     c1 = run_gemm(api, a, b, M, N, K, cta_group=1, tile_n=256)
     c2 = run_gemm(api, a, b, M, N, K, cta_group=2)
     assert torch.equal(c1, c2)
+
+
+@pytest.mark.parametrize("shape", [(16, 14336, 4096), (64, 4096, 14336), (128, 1024, 2048),
+                                   (1, 300, 512), (17, 1000, 96), (100, 2000, 4096),
+                                   (33, 256, 8192), (32, 4096, 14336), (8, 2048, 4096),
+                                   (16, 4096, 14336)])
+@pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
+def test_decode_kernel(api, orc, shape, out):
+    """M <= 128 (the weight-streaming split-K kernel where the heuristic picks it, else the
+    general kernel)."""
+    M, N, K = shape
+    _case(api, orc, M, N, K, seed=M + 3 * N + K, out=out)
+
+
+def test_decode_repeat_deterministic(api):
+    """Split-K partial sums are reduced in split order by the last CTA: repeated calls agree
+    bit for bit (and the per-tile counters reset themselves)."""
+    M, N, K = 16, 4096, 14336
+    _, a = make_operand(api, M, K, 41)
+    _, b = make_operand(api, N, K, 42)
+    c1 = run_gemm(api, a, b, M, N, K)
+    c2 = run_gemm(api, a, b, M, N, K)
+    c3 = run_gemm(api, a, b, M, N, K, out_dtype=torch.bfloat16)
+    assert torch.equal(c1, c2)
+    assert torch.equal(c1.to(torch.bfloat16), c3)
+
+
+def test_decode_matches_general_kernel(api):
+    M, N, K = 64, 2048, 4096
+    _, a = make_operand(api, M, K, 51)
+    _, b = make_operand(api, N, K, 52)
+    d = run_gemm(api, a, b, M, N, K)
+    g = run_gemm(api, a, b, M, N, K, cta_group=1, tile_n=128)
+    scale = g.abs().max().item()
+    assert (d - g).abs().max().item() <= 1e-5 * scale
