@@ -453,6 +453,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if ((it % kWriterGroups) != wgroup) continue;
         const int s = it % C::kStages;  // also the TMEM scale slot
         const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+        // First the slot (and the stage's previous use) must be free. Besides freeing the
+        // slot, this keeps "sfd" at most one phase ahead of this wait: the two writer groups
+        // alternate stages, so without it a group could wait on a stage whose previous fill
+        // has not landed yet, and a parity wait cannot tell that phase from its own.
+        if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word, kErrWaitSfEmpty)) {
+          ok = false;
+          break;
+        }
         if (!mbar_wait(smem_u32(&sfd[s]), j & 1u, abort_flag, p.err_word, kErrWaitTmaFull)) {
           ok = false;
           break;
@@ -471,11 +479,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const int o = kb * C::kSfbColsPerKb + 4 * jb;
             vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
           }
-        }
-        // The slot is free once the MMAs of the stage that last used it completed.
-        if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word, kErrWaitSfEmpty)) {
-          ok = false;
-          break;
         }
         tc_fence_after();
         const uint32_t sf_t = lane_base + C::kSfCol + s * kSfSlotCols;
@@ -755,6 +758,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if ((it % kWriterGroups) != wgroup) continue;
         const int s = it % C::kStages;
         const int slot = it % C::kSfSlots;
+        // Keep "sfd" at most one phase ahead of this wait (the writer groups alternate stages):
+        // the stage's previous use must have been consumed first.
+        if (!mbar_wait_cluster(smem_u32(&empty[s]),
+                               (static_cast<uint32_t>(it / C::kStages) & 1u) ^ 1u, abort_flag,
+                               p.err_word, kErrWaitSfEmpty)) {
+          ok = false;
+          break;
+        }
         if (!mbar_wait(smem_u32(&sfd[s]), static_cast<uint32_t>(it / C::kStages) & 1u, abort_flag,
                        p.err_word, kErrWaitTmaFull)) {
           ok = false;

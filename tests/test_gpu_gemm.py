@@ -151,3 +151,23 @@ def test_decode_matches_general_kernel(api):
     g = run_gemm(api, a, b, M, N, K, cta_group=1, tile_n=128)
     scale = g.abs().max().item()
     assert (d - g).abs().max().item() <= 1e-5 * scale
+
+
+@pytest.mark.parametrize("cta_group", [1, 2])
+def test_fresh_operand_buffers_reproduce(api, cta_group):
+    """Regression: launches on freshly written operand copies (slow first-touch loads) must
+    reproduce the first result bit for bit. This caught a scale-writer race in which one
+    writer group consumed a stage's scales before the bytes had landed."""
+    M, N, K = 4096, 14336, 4096
+    _, a = make_operand(api, M, K, 1234)
+    _, b = make_operand(api, N, K, 1234 ^ 0xABCDEF)
+    ref = run_gemm(api, a, b, M, N, K, out_dtype=torch.bfloat16, cta_group=cta_group, tile_n=256)
+    for _ in range(6):
+        a2 = api.Nvfp4Tensor(a.rows, a.cols, a.global_scale, a.packed.clone(), a.scales.clone(),
+                             a.scales_tc.clone())
+        b2 = api.Nvfp4Tensor(b.rows, b.cols, b.global_scale, b.packed.clone(), b.scales.clone(),
+                             b.scales_tc.clone())
+        got = run_gemm(api, a2, b2, M, N, K, out_dtype=torch.bfloat16, cta_group=cta_group,
+                       tile_n=256)
+        assert torch.equal(got, ref)
+        del a2, b2
