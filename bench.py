@@ -181,6 +181,7 @@ def run_b200(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     from nvfp4bench_b200 import api
+    from nvfp4bench_b200.shard import max_over_ranks, shard_bounds
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -189,8 +190,11 @@ def run_b200(args, rank, world, local_rank):
     out_bytes = 2 if od == "bf16" else 4
     stream = torch.cuda.current_stream()
 
-    # Operands: A replicated (same seed on every rank), B = this rank's N-slice of a
-    # world*N-wide weight (seed offset by rank).
+    # Operands: A replicated (same seed on every rank), B = this rank's N-slice
+    # [n0, n1) = shard_bounds(world*N, world, rank) of a world*N-wide weight, drawn with the
+    # weight seed offset by the rank.
+    n0, n1 = shard_bounds(world * N, world, rank)
+    assert n1 - n0 == N
     x = api.fill_normal(M, K, SEED_A)
     A = api.quantize(x, canonical=False, tcgen05=True)
     del x
@@ -239,10 +243,7 @@ def run_b200(args, rank, world, local_rank):
     times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     mean_ms = sum(times) / len(times)
     min_ms, med_ms = min(times), statistics.median(times)
-    t = torch.tensor([mean_ms, min_ms, med_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    mean_ms, min_ms, med_ms = t.tolist()
+    mean_ms, min_ms, med_ms = max_over_ranks([mean_ms, min_ms, med_ms], device=dev)
     derr = api.device_error()
     if derr:
         raise RuntimeError(f"device error word {derr:#x}")
@@ -300,10 +301,7 @@ def run_b200(args, rank, world, local_rank):
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = e2e_ms.item()
+    e2e_ms = max_over_ranks([e0.elapsed_time(e1) / args.steps], device=dev)[0]
     if not torch.equal(hC.to(dev), C):
         raise RuntimeError("e2e output differs from the device-resident output")
 

@@ -1,0 +1,45 @@
+"""N-sharding of the GEMM across ranks (one process per GPU).
+
+D = A * B^T is split along N: rank r owns weight rows [n0, n1) of B (and the matching
+columns of D); A is replicated. The GEMM needs no communication; the only collective is the
+max-over-ranks reduction of step times (and, optionally, an all-gather of the D shards).
+"""
+from __future__ import annotations
+
+from typing import Tuple
+
+
+def shard_bounds(n_total: int, world: int, rank: int, align: int = 128) -> Tuple[int, int]:
+    """Contiguous [n0, n1) slice of n_total rows for `rank`, in whole `align`-row blocks
+    (the kernels' tile height) except for the last rank, which takes the remainder."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad world/rank")
+    blocks = (n_total + align - 1) // align
+    b0 = blocks * rank // world
+    b1 = blocks * (rank + 1) // world
+    return min(b0 * align, n_total), min(b1 * align, n_total)
+
+
+def max_over_ranks(values, device=None):
+    """Element-wise max of a list of floats over all ranks (identity without a process group)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def gather_columns(local, n_total: int, device=None):
+    """All-gather of per-rank column shards [M][n1-n0] into the full [M][n_total] matrix."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size()
+    M = local.shape[0]
+    spans = [shard_bounds(n_total, world, r) for r in range(world)]
+    width = max(n1 - n0 for n0, n1 in spans)  # collectives want equal sizes: pad, then trim
+    padded = torch.zeros((M, width), dtype=local.dtype, device=local.device)
+    padded[:, : local.shape[1]] = local
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded)
+    return torch.cat([p[:, : n1 - n0] for p, (n0, n1) in zip(parts, spans)], dim=1)
