@@ -278,3 +278,26 @@ bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStr
 }
 
 }  // namespace nvfp4b200
+
+// ---- GPU mirror of the reference oracle (src/reference.cu:9-17) for the C++ harness's
+// --validate: C[m][n] = sum_k A[m][k] * B[n][k] in FP32, k ascending, one thread per output.
+namespace nvfp4b200 {
+namespace {
+__global__ void naive_gemm_nt_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                     float* __restrict__ C, int M, int N, int K) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y * blockDim.y + threadIdx.y;
+  if (m >= M || n >= N) return;
+  float acc = 0.0f;
+  for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __fmul_rn(A[static_cast<size_t>(m) * K + k],
+                                                            B[static_cast<size_t>(n) * K + k]));
+  C[static_cast<size_t>(m) * N + n] = acc;
+}
+}  // namespace
+
+bool naive_gemm_nt(const float* A, const float* B, int M, int N, int K, float* C, cudaStream_t s,
+                   std::string* err) {
+  dim3 block(16, 16), grid((N + 15) / 16, (M + 15) / 16);
+  naive_gemm_nt_kernel<<<grid, block, 0, s>>>(A, B, C, M, N, K);
+  return check_launch("naive_gemm_nt", err);
+}
+}  // namespace nvfp4b200

@@ -45,6 +45,9 @@ bool dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols
                 float global_scale, float* out, cudaStream_t s, std::string* err);
 bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStream_t s,
                    std::string* err);
+// GPU mirror of the reference's naive FP32 oracle (src/reference.cu:9-17) with B as N x K.
+bool naive_gemm_nt(const float* A, const float* B, int M, int N, int K, float* C, cudaStream_t s,
+                   std::string* err);
 
 // ---- roofs (roofs.cu) ----------------------------------------------------------------
 bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, size_t bytes,
