@@ -291,6 +291,14 @@ double run_ladder(const Dev& dev, bool print) {
                   dev.sms, tf);
     best = std::max(best, tf);
   }
+  double tf2 = 0;
+  if (nvfp4b200::peak_ladder_pair(256, dev.sms / 2, 4096, 10, &tf2, 0, &err)) {
+    if (print)
+      std::printf("tcgen05 kind::mxf4nvf4 block_scale cta_group::2 M256 x N256 x K64, %d SM pairs: %8.1f TFLOPS\n",
+                  dev.sms / 2, tf2);
+  } else if (print) {
+    std::printf("pair rung failed: %s\n", err.c_str());
+  }
   return best;
 }
 

@@ -54,5 +54,8 @@ bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, s
                        int iters, double* gbs, cudaStream_t s, std::string* err);
 bool peak_ladder(int n, int ctas, int iters, int reps, double* tflops, cudaStream_t s,
                  std::string* err);
+// SM-pair rung: `clusters` clusters of 2 CTAs, cta_group::2 MMAs of M=256 x n x K=64.
+bool peak_ladder_pair(int n, int clusters, int iters, int reps, double* tflops, cudaStream_t s,
+                      std::string* err);
 
 }  // namespace nvfp4b200

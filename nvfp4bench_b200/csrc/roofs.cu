@@ -94,7 +94,118 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32
   if (threadIdx.x < 32) tmem_dealloc(tbase, 512);
 }
 
+// SM-pair rung: clusters of two CTAs; the leader issues M=256 x N x K=64 MMAs with
+// cta_group::2 (each SM computes 128 x N), both CTAs allocate TMEM and hold scale copies.
+template <int N>
+__global__ void __launch_bounds__(kPeakThreads, 1) peak_pair_kernel(int iters, uint32_t* err_word) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  constexpr int kA = 128 * 128, kB = (N / 2) * 128, kSf = 4096;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kA + kB + kSf);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  for (int i = threadIdx.x; i < (kA + kB) / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(bar), 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x < 32) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  // Unit scales (0x38) into TMEM rows of both CTAs by their own threads.
+  if (threadIdx.x < 128) {
+    const int q = threadIdx.x >> 5;
+    const uint32_t lb = tbase + (static_cast<uint32_t>(q * 32) << 16) + 448;
+    uint32_t v[16];
+    for (int i = 0; i < 16; ++i) v[i] = 0x38383838u;
+    tmem_st_32x32b_x16(lb, v);
+    tc_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  if (threadIdx.x == 0 && cluster_ctarank() == 0) {
+    const uint32_t a_s = smem_u32(smem), b_s = smem_u32(smem + kA);
+    const uint32_t idesc = make_idesc_mxf4nvf4(256, N);
+    const uint64_t ad = make_sdesc(a_s, 16, 1024, 2), bd = make_sdesc(b_s, 16, 1024, 2);
+    for (int i = 0; i < iters; ++i)
+      tc_mma_mxf4nvf4_pair(tbase, ad, bd, idesc, tbase + 448, tbase + 452, i > 0);
+    tc_commit_pair(smem_u32(bar));
+    volatile int never = 0;
+    mbar_wait(smem_u32(bar), 0, &never, err_word, kErrWaitDrain);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc_pair(tbase, 512);
+}
+
 }  // namespace
+
+bool peak_ladder_pair(int n, int clusters, int iters, int reps, double* tflops, cudaStream_t s,
+                      std::string* err) {
+  if (n != 256 || clusters < 1 || iters < 1 || reps < 1 || !tflops) {
+    set_err(err, "peak (pair): n must be 256, clusters/iters/reps >= 1");
+    return false;
+  }
+  uint32_t* ew = device_error_word(err);
+  if (!ew) return false;
+  const int smem = 1024 + 128 * 128 + 128 * 128 + 4096 + 64;
+  cudaError_t e = cudaFuncSetAttribute(peak_pair_kernel<256>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_err(err, std::string("peak pair attr: ") + cudaGetErrorString(e));
+    return false;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(kPeakThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto launch = [&]() { return cudaLaunchKernelEx(&cfg, peak_pair_kernel<256>, iters, ew); };
+  if ((e = launch()) != cudaSuccess) {
+    set_err(err, std::string("peak pair launch: ") + cudaGetErrorString(e));
+    return false;
+  }
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  float best = 1e30f;
+  for (int r = 0; r < reps; ++r) {
+    cudaEventRecord(a, s);
+    launch();
+    cudaEventRecord(b, s);
+    cudaEventSynchronize(b);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    best = std::min(best, ms);
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(err, std::string("peak pair: ") + cudaGetErrorString(e));
+    return false;
+  }
+  *tflops = 2.0 * 256.0 * n * 64.0 * static_cast<double>(clusters) * iters / (best * 1e-3) / 1e12;
+  return true;
+}
 
 bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, size_t bytes,
                        int iters, double* gbs, cudaStream_t s, std::string* err) {
