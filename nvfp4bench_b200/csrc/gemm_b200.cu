@@ -8,8 +8,8 @@
 //
 // Kernel design (one persistent CTA per SM, 448 threads):
 //   warp 0      TMA producer: per K-stage, two tiled TMA loads (A 128 x 256 FP4, B BN x 256
-//               FP4, both 128-byte-swizzled K-major) and 1-D bulk copies of the scale atoms,
-//               all completing on one mbarrier ("full"). No multicast.
+//               FP4, both 128-byte-swizzled K-major) completing on one mbarrier ("full").
+//               Four 48 KB stages (BN = 256) or six 32 KB stages (BN = 128). No multicast.
 //   warp 1      MMA issuer (one lane): per K-stage, four tcgen05.mma kind::mxf4nvf4
 //               block_scale (M=128, N=BN, K=64) back to back. tcgen05.commit frees the scale
 //               slot ("sf_empty") and the smem stage ("empty") and, per tile, publishes the
@@ -19,22 +19,24 @@
 //               tile and store it with one TMA tensor store (clipped at the matrix edges).
 //               Warp w reads TMEM lane quadrant w % 4. Outputs whose row pitch is not a
 //               multiple of 16 bytes fall back to per-thread global stores.
-//   warps 6..13 scale writers, two per TMEM quadrant taking even and odd stages in turn
-//               (one writer's per-stage latency exceeds a stage's 512 MMA cycles): per K-stage,
-//               each copies the stage's scale atoms from shared
-//               memory into a ring of three scale slots in TMEM with tcgen05.st (one batched
-//               store per stage: a cross-warp mbarrier round trip costs ~390 cycles, so a
-//               per-K-block handshake would be slower than the 128-cycle MMA it feeds). Each warp writes its
-//               own 32-lane quadrant, so the four quadrants hold identical copies: the layout
-//               the block-scaled MMA reads. tcgen05.cp would do the same copy on the tensor
-//               pipe, in series with the MMAs (measured on B200: 4 MMAs of a stage take 512
-//               cycles, 980 with the stage's 12 copies); tcgen05.st from these warps runs
-//               beside the MMAs.
+//   warps 6..13 scale writers, two per TMEM quadrant taking even and odd stages in turn:
+//               per K-stage each loads its lanes' 16 bytes of the stage's scale atoms from
+//               global memory (L2) into registers and writes them with tcgen05.st into a
+//               ring of two scale slots in TMEM (one batched store per stage: a cross-warp
+//               mbarrier round trip costs ~390 cycles, more than the 128-cycle MMA a
+//               per-K-block handshake would feed). Each warp writes its own 32-lane quadrant,
+//               so the four quadrants hold identical copies: the layout the block-scaled MMA
+//               reads. tcgen05.cp would do the same copy on the tensor pipe, in series with
+//               the MMAs (measured on B200: 4 MMAs of a stage take 512 cycles, 980 with the
+//               stage's 12 copies); tcgen05.st from these warps runs beside the MMAs. Scales
+//               take no shared memory, which leaves room for a fourth A/B stage: the kernel is
+//               bound by L2-to-shared-memory throughput, and the deeper ring keeps more bytes
+//               in flight.
 // Two accumulator buffers let the epilogue of tile i overlap the MMAs of tile i+1. With
-// BN = 256 the two 256-column buffers and the 144 scale columns do not fit the 512 TMEM
-// columns side by side, so buffer 1 starts at column 112: the epilogue loads the 5 chunks
-// that hold the 144 shared columns first, releases them ("acc_early") as soon as they are in registers, and drains
-// the rest afterwards.
+// BN = 256 the two 256-column buffers and the 96 scale columns do not fit the 512 TMEM
+// columns side by side, so buffer 1 starts at column 160: the epilogue loads the 3 chunks
+// that hold the 96 shared columns first, releases them ("acc_early") as soon as they are in
+// registers, and drains the rest afterwards.
 //
 // Every mbarrier wait is bounded (ptx.cuh); a timeout sets the device error word, all roles
 // leave their loops, in-flight copies and MMAs are drained with bounded waits, TMEM is freed
@@ -67,23 +69,25 @@ constexpr int kWriterGroups = 2;  // scale writers: two warps per TMEM quadrant,
 constexpr int kTmemCols = 512;
 constexpr int kSfSlotCols = 48;   // per stage: SFA at +4*kb (16 columns), SFB at +16 + 8*kb
 constexpr int kSfbOff = 16;
+#ifndef NVFP4_SF_SLOTS
+#define NVFP4_SF_SLOTS 2
+#endif
 
 template <int BN>
 struct Cfg {
   static constexpr int kABytes = kBM * kBKBytes;                 // 16 KB
   static constexpr int kBBytes = BN * kBKBytes;                  // 16 / 32 KB
-  static constexpr int kSfaBytes = kKBlocksPerStage * 512;       // 2 KB
-  static constexpr int kSfbBytes = (BN + 127) / 128 * kKBlocksPerStage * 512;
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kStages = (BN == 256) ? 3 : 5;
+  static constexpr int kStageBytes = kABytes + kBBytes;          // scales bypass smem
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
   static constexpr int kCBufBytes = 32 * 32 * 4;                // one FP32 32 x 32 chunk
   static constexpr int kCBytes = 4 * 2 * kCBufBytes;            // 4 warps, double-buffered
   static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
-  // TMEM: one scale slot per smem stage (so a stage's "empty" also frees its slot) at the top,
-  // two accumulator buffers below; which 32-column chunks the buffers share.
-  static constexpr int kSfSlots = kStages;
-  static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368 / 272
+  // TMEM: a ring of scale slots at the top (freed by "sf_empty", independent of the smem
+  // stages), two accumulator buffers below; which 32-column chunks the buffers share.
+  static constexpr int kSfSlots = NVFP4_SF_SLOTS;
+  static_assert(kSfSlots <= kStages, "a writer's slot wait must also order its full[] arrival");
+  static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368
   static constexpr int kAccBase1 = (BN == 256) ? kSfCol - 256 : BN;  // 112 for BN = 256
   static constexpr int kChunks = BN / 32;
   static constexpr bool kOverlap = (BN == 256);
@@ -93,7 +97,7 @@ struct Cfg {
   static constexpr int kSfbColsPerKb = kSfbAtoms * 4;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kAccBase1 + BN <= kSfCol && kAccBase1 >= 0, "TMEM budget");
-  static_assert(!kOverlap || (kOverlapChunks >= 4 && kOverlapChunks <= 6), "overlap chunks");
+  static_assert(!kOverlap || (kOverlapChunks >= 3 && kOverlapChunks <= 6), "overlap chunks");
 };
 
 struct GemmParams {
@@ -254,6 +258,13 @@ __device__ __forceinline__ void drain_overlapped(const GemmParams& p, EpiStage& 
   const int o = b ? 0 : 8 - OV;
   const int rest = b ? OV : 0;
   const int g0[3] = {o, o + 1, o + 2};
+  if constexpr (OV == 3) {
+    const int g1[3] = {rest, rest + 1, rest + 2}, g2[2] = {rest + 3, rest + 4};
+    epi_group<3, kRemote>(p, e, acc_t, g0, row, col_base, early_bar);
+    epi_group<3>(p, e, acc_t, g1, row, col_base, 0);
+    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
+    return;
+  }
   epi_group<3>(p, e, acc_t, g0, row, col_base, 0);
   if constexpr (OV == 6) {
     const int g1[3] = {o + 3, o + 4, o + 5}, g2[2] = {rest, rest + 1};
@@ -283,14 +294,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + C::kStages * C::kABytes;
-  uint8_t* sSFA = sB + C::kStages * C::kBBytes;
-  uint8_t* sSFB = sSFA + C::kStages * C::kSfaBytes;
-  uint8_t* sC = sSFB + C::kStages * C::kSfbBytes;  // 1024-aligned: stages are multiples of 1 KB
+  uint8_t* sC = sB + C::kStages * C::kBBytes;  // 1024-aligned: stages are multiples of 1 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
   uint64_t* full = bars;                // A/B bytes + producer + the stage's 4 scale writers
-  uint64_t* empty = bars + C::kStages;  // stage (smem and its TMEM scale slot) consumed
-  uint64_t* sfd = empty + C::kStages;   // the stage's scale bytes landed in smem
-  uint64_t* acc_full = sfd + C::kStages;
+  uint64_t* empty = bars + C::kStages;  // smem stage consumed
+  uint64_t* sf_empty = empty + C::kStages;  // TMEM scale slot consumed
+  uint64_t* acc_full = sf_empty + C::kSfSlots;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* acc_early = acc_full + 4;
   uint64_t* drain = acc_full + 6;
@@ -304,8 +313,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(smem_u32(&full[s]), 1 + 4);
       mbar_init(smem_u32(&empty[s]), 1);
-      mbar_init(smem_u32(&sfd[s]), 1);
     }
+    for (int j = 0; j < C::kSfSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&acc_empty[b]), 4);
@@ -344,22 +353,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             ok = false;
             break;
           }
-          int nkb = p.ka - kt * kKBlocksPerStage;
-          if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
-          const uint32_t sf_bytes = static_cast<uint32_t>(nkb) * 512u;
-          int nsfb = 0;
-          for (int jb = 0; jb < (BN + 127) / 128; ++jb)
-            if (n0 / 128 + jb < p.sfb_rowblocks) ++nsfb;
-          const uint32_t db = smem_u32(&sfd[s]);
-          mbar_arrive_expect_tx(db, sf_bytes * (1 + nsfb));
-          bulk_load(smem_u32(sSFA + s * C::kSfaBytes),
-                    p.sfa + (static_cast<size_t>(tm) * p.ka + kt * kKBlocksPerStage) * 512,
-                    sf_bytes, db);
-          for (int jb = 0; jb < nsfb; ++jb) {
-            const size_t rb = static_cast<size_t>(n0 / 128 + jb);
-            bulk_load(smem_u32(sSFB + s * C::kSfbBytes + jb * kKBlocksPerStage * 512),
-                      p.sfb + (rb * p.ka + kt * kKBlocksPerStage) * 512, sf_bytes, db);
-          }
           const uint32_t fb = smem_u32(&full[s]);
           mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes);
           tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * kBKBytes, m0, fb);
@@ -367,10 +360,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       }
       if (!ok) {
-        // Drain: the most recent fill of every stage must land before the CTA exits.
+        // Drain: the most recent fill of every stage must land before the CTA exits. "full"
+        // also counts the scale writers, which may have left early; the bounded wait then
+        // gives the copies far longer than they take.
         for (int back = 1; back <= C::kStages && it - back >= 0; ++back) {
           const int f = it - back;
-          mbar_wait_drain(smem_u32(&sfd[f % C::kStages]),
+          mbar_wait_drain(smem_u32(&full[f % C::kStages]),
                           static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
         }
       }
@@ -416,7 +411,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           // Descriptor start addresses are in 16-byte units: +2 per 32-byte K-block.
           const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 1024, 2);
           const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
-          const uint32_t sf_t = tmem_base + C::kSfCol + s * kSfSlotCols;
+          const int slot = it % C::kSfSlots;
+          const uint32_t sf_t = tmem_base + C::kSfCol + slot * kSfSlotCols;
           if (nkb == kKBlocksPerStage) {
 #pragma unroll
             for (int kb = 0; kb < kKBlocksPerStage; ++kb)
@@ -428,6 +424,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                               sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
           }
           issued = true;
+          tc_commit(smem_u32(&sf_empty[slot]));
           tc_commit(smem_u32(&empty[s]));
         }
         if (!ok) break;
@@ -441,47 +438,56 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else if (warp >= 6) {
     // ------------------------------------------------------------------ scale writers
     // In an atom, lane l's 16 bytes are 4 words; word g holds the 4 K-scales of row 32g + l.
-    // Slot columns: SFA K-block kb's words at +4*kb, SFB atom jb of K-block kb at
-    // +16 + kb*(4*atoms) + 4*jb. K-blocks past the end of K keep stale words no MMA reads.
+    // Each writer reads its lanes' words of the stage's atoms straight from global memory (L2)
+    // into registers, so scales take no shared memory and no copy of their own. Slot columns:
+    // SFA K-block kb's words at +4*kb, SFB atom jb of K-block kb at +16 + kb*(4*atoms) + 4*jb.
+    // K-blocks past the end of K and atoms past the last row block are written as zero
+    // scales; no output the kernel stores depends on them.
     const int q = warp & 3;
     const int wgroup = (warp - 6) >> 2;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      const uint8_t* ga = p.sfa + static_cast<size_t>(tm) * p.ka * 512 + lane * 16;
       for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
         if ((it % kWriterGroups) != wgroup) continue;
-        const int s = it % C::kStages;  // also the TMEM scale slot
-        const uint32_t j = static_cast<uint32_t>(it / C::kStages);
-        // First the slot (and the stage's previous use) must be free. Besides freeing the
-        // slot, this keeps "sfd" at most one phase ahead of this wait: the two writer groups
-        // alternate stages, so without it a group could wait on a stage whose previous fill
-        // has not landed yet, and a parity wait cannot tell that phase from its own.
-        if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word, kErrWaitSfEmpty)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(smem_u32(&sfd[s]), j & 1u, abort_flag, p.err_word, kErrWaitTmaFull)) {
-          ok = false;
-          break;
-        }
-        const uint8_t* sfa_s = sSFA + s * C::kSfaBytes + lane * 16;
-        const uint8_t* sfb_s = sSFB + s * C::kSfbBytes + lane * 16;
-        uint32_t va[16], vb[32];
+        const int s = it % C::kStages;
+        const int slot = it % C::kSfSlots;
+        int nkb = p.ka - kt * kKBlocksPerStage;
+        if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+        uint32_t va[16], vb[4 * C::kSfbColsPerKb];
 #pragma unroll
         for (int kb = 0; kb < kKBlocksPerStage; ++kb) {
-          const uint4 w = *reinterpret_cast<const uint4*>(sfa_s + kb * 512);
+          uint4 w = make_uint4(0u, 0u, 0u, 0u);
+          if (kb < nkb)
+            w = __ldg(reinterpret_cast<const uint4*>(ga + (kt * kKBlocksPerStage + kb) * 512));
           va[4 * kb + 0] = w.x; va[4 * kb + 1] = w.y; va[4 * kb + 2] = w.z; va[4 * kb + 3] = w.w;
 #pragma unroll
           for (int jb = 0; jb < C::kSfbAtoms; ++jb) {
-            const uint4 x =
-                *reinterpret_cast<const uint4*>(sfb_s + jb * kKBlocksPerStage * 512 + kb * 512);
+            const int rb = tn * (BN / 128) + jb;
+            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            if (kb < nkb && rb < p.sfb_rowblocks)
+              x = __ldg(reinterpret_cast<const uint4*>(
+                  p.sfb + (static_cast<size_t>(rb) * p.ka + kt * kKBlocksPerStage + kb) * 512 +
+                  lane * 16));
             const int o = kb * C::kSfbColsPerKb + 4 * jb;
             vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
           }
         }
+        // The slot's previous use (stage it - kSfSlots) must have been consumed. This also
+        // orders this writer's "full" arrival after that barrier's previous phase, because
+        // kSfSlots <= kStages.
+        if (!mbar_wait(smem_u32(&sf_empty[slot]),
+                       (static_cast<uint32_t>(it / C::kSfSlots) & 1u) ^ 1u, abort_flag,
+                       p.err_word, kErrWaitSfEmpty)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t sf_t = lane_base + C::kSfCol + s * kSfSlotCols;
+        const uint32_t sf_t = lane_base + C::kSfCol + slot * kSfSlotCols;
         tmem_st_32x32b_x16(sf_t, va);
         tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
         if (C::kSfbAtoms == 2) tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
