@@ -117,6 +117,16 @@ int nvfp4_b200_measure_bandwidth(int kind, const void* src, void* dst, const voi
 int nvfp4_b200_peak(int n, int ctas, int iters, int reps, double* tflops, void* stream,
                     char* err, size_t errlen);
 
+/* The same ladder with its options (src/peak.cu:119-156 has one fixed configuration):
+ * cta_group 1 runs `units` CTAs of M=128 x n MMAs (n 128 or 256), cta_group 2 runs `units`
+ * SM pairs of M=256 x 256 MMAs. seed 0 stages zero operands, any other value pseudo-random
+ * E2M1 bytes (the data sets the power drawn and so, under the power cap, the clock).
+ * sustained 0: best of `reps` single timed launches; 1: mean over `reps` back-to-back
+ * launches. *sm_mhz (may be NULL) gets the SM clock CTA 0 ran at (clock64 / globaltimer). */
+int nvfp4_b200_peak_ex(int n, int cta_group, int units, int iters, int reps, uint32_t seed,
+                       int sustained, double* tflops, double* sm_mhz, void* stream, char* err,
+                       size_t errlen);
+
 /* Reads (and when clear != 0 resets) the device error word the kernels write when a
  * bounded wait times out (bit meanings in nvfp4bench_b200/csrc/ptx.cuh). Synchronises
  * the current device. Returns 0 on success with the word in *word. */

@@ -29,7 +29,7 @@ EXPORTED = [
     "nvfp4_b200_fill_uniform", "nvfp4_b200_fill_normal", "nvfp4_b200_sf_tcgen05_bytes",
     "nvfp4_b200_sf_to_tcgen05", "nvfp4_b200_measure_bandwidth", "nvfp4_b200_peak",
     "nvfp4_b200_device_error", "nvfp4_b200_wait_selftest", "nvfp4_b200_version",
-    "nvfp4_b200_gemm_noalloc", "nvfp4_b200_gemm_noalloc_scratch_bytes",
+    "nvfp4_b200_gemm_noalloc", "nvfp4_b200_gemm_noalloc_scratch_bytes", "nvfp4_b200_peak_ex",
 ]
 
 
@@ -211,6 +211,16 @@ def peak(n: int = 256, ctas: int = 148, iters: int = 4096, reps: int = 5, stream
     t = C.c_double(0.0)
     _call(lib().nvfp4_b200_peak, n, ctas, iters, reps, C.byref(t), _stream(stream))
     return t.value
+
+
+def peak_ex(n: int = 256, cta_group: int = 1, units: int = 148, iters: int = 4096, reps: int = 5,
+            seed: int = 0, sustained: bool = False, stream=None) -> tuple:
+    """(TFLOP/s, SM MHz of CTA 0) of one ladder rung; see nvfp4_b200_peak_ex."""
+    t = C.c_double(0.0)
+    mhz = C.c_double(0.0)
+    _call(lib().nvfp4_b200_peak_ex, n, cta_group, units, iters, reps, C.c_uint32(seed),
+          1 if sustained else 0, C.byref(t), C.byref(mhz), _stream(stream))
+    return t.value, mhz.value
 
 
 def device_error(clear: bool = True) -> int:

@@ -190,6 +190,16 @@ int nvfp4_b200_peak(int n, int ctas, int iters, int reps, double* tflops, void* 
   return ok(err, errlen);
 }
 
+int nvfp4_b200_peak_ex(int n, int cta_group, int units, int iters, int reps, uint32_t seed,
+                       int sustained, double* tflops, double* sm_mhz, void* stream, char* err,
+                       size_t errlen) {
+  std::string e;
+  const nvfp4b200::PeakOptions o{n, cta_group, units, iters, reps, seed, sustained};
+  if (!nvfp4b200::peak_ladder_ex(o, tflops, sm_mhz, static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
 int nvfp4_b200_device_error(int clear, uint32_t* word, char* err, size_t errlen) {
   std::string e;
   uint32_t* ew = nvfp4b200::device_error_word(&e);

@@ -24,14 +24,18 @@
 //               global memory (L2) into registers and writes them with tcgen05.st into a
 //               ring of two scale slots in TMEM (one batched store per stage: a cross-warp
 //               mbarrier round trip costs ~390 cycles, more than the 128-cycle MMA a
-//               per-K-block handshake would feed). Each warp writes its own 32-lane quadrant,
-//               so the four quadrants hold identical copies: the layout the block-scaled MMA
-//               reads. tcgen05.cp would do the same copy on the tensor pipe, in series with
-//               the MMAs (measured on B200: 4 MMAs of a stage take 512 cycles, 980 with the
-//               stage's 12 copies); tcgen05.st from these warps runs beside the MMAs. Scales
-//               take no shared memory, which leaves room for a fourth A/B stage: the kernel is
-//               bound by L2-to-shared-memory throughput, and the deeper ring keeps more bytes
-//               in flight.
+//               per-K-block handshake would feed). Each warp writes its own 32-lane quadrant.
+//               SFB rows map to accumulator columns, which every quadrant computes, so SFB is
+//               stored whole in all four quadrants (the layout tcgen05.cp .warpx4 produces);
+//               SFA rows map to TMEM lanes, and the MMA rows of quadrant q read only column q
+//               of each 4-column SFA group, so each writer stores just that column (a quarter
+//               of the bytes; verified bit-exact by the integer known-answer test).
+//               TMEM stores from other warps slow the MMAs that share the TMEM (measured: 16%
+//               faster with no scale stores at all), so fewer bytes is faster. tcgen05.cp
+//               would do the copy on the tensor pipe, in series with the MMAs (4 MMAs of a
+//               stage take 512 cycles, 980 with the stage's 12 copies). Scales take no shared
+//               memory, which leaves room for a fourth A/B stage: more bytes in flight for the
+//               L2-to-shared-memory stream.
 // Two accumulator buffers let the epilogue of tile i overlap the MMAs of tile i+1. With
 // BN = 256 the two 256-column buffers and the 96 scale columns do not fit the 512 TMEM
 // columns side by side, so buffer 1 starts at column 160: the epilogue loads the 3 chunks
@@ -458,13 +462,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int slot = it % C::kSfSlots;
         int nkb = p.ka - kt * kKBlocksPerStage;
         if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
-        uint32_t va[16], vb[4 * C::kSfbColsPerKb];
+        // SFA: only word q of each atom row (the 4 K-scales of row 32q + lane) is read by the
+        // MMA rows of quadrant q, so each writer stores that one column per K-block. SFB rows
+        // map to accumulator columns, which every quadrant computes: all four words, in every
+        // quadrant.
+        uint32_t va[kKBlocksPerStage], vb[4 * C::kSfbColsPerKb];
 #pragma unroll
         for (int kb = 0; kb < kKBlocksPerStage; ++kb) {
-          uint4 w = make_uint4(0u, 0u, 0u, 0u);
+          va[kb] = 0u;
           if (kb < nkb)
-            w = __ldg(reinterpret_cast<const uint4*>(ga + (kt * kKBlocksPerStage + kb) * 512));
-          va[4 * kb + 0] = w.x; va[4 * kb + 1] = w.y; va[4 * kb + 2] = w.z; va[4 * kb + 3] = w.w;
+            va[kb] = __ldg(reinterpret_cast<const uint32_t*>(ga + q * 4 + (kt * kKBlocksPerStage + kb) * 512));
 #pragma unroll
           for (int jb = 0; jb < C::kSfbAtoms; ++jb) {
             const int rb = tn * (BN / 128) + jb;
@@ -488,7 +495,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         tc_fence_after();
         const uint32_t sf_t = lane_base + C::kSfCol + slot * kSfSlotCols;
-        tmem_st_32x32b_x16(sf_t, va);
+#pragma unroll
+        for (int kb = 0; kb < kKBlocksPerStage; ++kb) tmem_st_32x32b_x1(sf_t + kb * 4 + q, va[kb]);
         tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
         if (C::kSfbAtoms == 2) tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
         tc_wait_st();
@@ -556,19 +564,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 struct PairCfg {
   static constexpr int kABytes = 128 * kBKBytes;       // this CTA's 128 rows of A
   static constexpr int kBBytes = 128 * kBKBytes;       // this CTA's 128 rows of B
-  static constexpr int kSfaBytes = kKBlocksPerStage * 512;
-  static constexpr int kSfbBytes = 2 * kKBlocksPerStage * 512;  // all 256 rows of B
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 38 KB
-  static constexpr int kStages = 5;
+  static constexpr int kStageBytes = kABytes + kBBytes;  // 32 KB; scales bypass smem
+  static constexpr int kStages = 6;
   static constexpr int kCBufBytes = 32 * 32 * 4;
   static constexpr int kCBytes = 4 * 2 * kCBufBytes;
   static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
-  static constexpr int kSfSlots = 3;                    // ring of per-stage scale slots
-  static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368
-  static constexpr int kAccBase1 = kSfCol - 256;       // 112, as in the one-SM N=256 kernel
+  static constexpr int kSfSlots = NVFP4_SF_SLOTS;       // ring of per-stage scale slots
+  static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;
+  static constexpr int kAccBase1 = kSfCol - 256;       // as in the one-SM N=256 kernel
   static constexpr int kOverlapChunks = (256 - kAccBase1 + 31) / 32;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kSfSlots <= kStages, "a writer's slot wait must also order its full[] arrival");
 };
 
 __global__ void __launch_bounds__(kNumThreads, 1)
@@ -581,14 +588,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + C::kStages * C::kABytes;
-  uint8_t* sSFA = sB + C::kStages * C::kBBytes;
-  uint8_t* sSFB = sSFA + C::kStages * C::kSfaBytes;
-  uint8_t* sC = sSFB + C::kStages * C::kSfbBytes;
+  uint8_t* sC = sB + C::kStages * C::kBBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
   uint64_t* full = bars;                    // leader: A/B bytes of both CTAs
   uint64_t* empty = full + C::kStages;      // each CTA: stage consumed
-  uint64_t* sfd = empty + C::kStages;       // each CTA: its scale bytes landed
-  uint64_t* acc_full = sfd + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;       // leader, 8 arrivals
   uint64_t* acc_early = acc_full + 4;       // leader, 8 arrivals
   uint64_t* sf_empty = acc_full + 6;        // each CTA: scale slot consumed
@@ -607,7 +611,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(smem_u32(&full[s]), 1 + 8);  // leader's expect_tx + both CTAs' scale writers
       mbar_init(smem_u32(&empty[s]), 1);
-      mbar_init(smem_u32(&sfd[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
@@ -642,7 +645,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         int tm, tn;
         tile_coords(p, t, tm, tn);
         const int m0 = tm * 256 + static_cast<int>(rank) * 128, n0 = tn * 256;
-        const bool sfa_ok = (m0 / 128) < p.sfa_rowblocks;
         for (int kt = 0; kt < p.num_kt; ++kt, ++it) {
           const int s = it % C::kStages;
           const uint32_t j = static_cast<uint32_t>(it / C::kStages);
@@ -651,35 +653,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             ok = false;
             break;
           }
-          int nkb = p.ka - kt * kKBlocksPerStage;
-          if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
-          const uint32_t sf_bytes = static_cast<uint32_t>(nkb) * 512u;
-          int nsfb = 0;
-          for (int jb = 0; jb < 2; ++jb)
-            if (n0 / 128 + jb < p.sfb_rowblocks) ++nsfb;
           if (rank == 0) mbar_arrive_expect_tx(smem_u32(&full[s]), 2 * (C::kABytes + C::kBBytes));
           const uint32_t fb = full_l0 + s * 8;
           tma_load_2d_pair(smem_u32(sA + s * C::kABytes), &tmap_a, kt * kBKBytes, m0, fb);
           tma_load_2d_pair(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes,
                            n0 + static_cast<int>(rank) * 128, fb);
-          const uint32_t db = smem_u32(&sfd[s]);
-          mbar_arrive_expect_tx(db, sf_bytes * ((sfa_ok ? 1 : 0) + nsfb));
-          if (sfa_ok)
-            bulk_load(smem_u32(sSFA + s * C::kSfaBytes),
-                      p.sfa + (static_cast<size_t>(m0 / 128) * p.ka + kt * kKBlocksPerStage) * 512,
-                      sf_bytes, db);
-          for (int jb = 0; jb < nsfb; ++jb) {
-            const size_t rb = static_cast<size_t>(n0 / 128 + jb);
-            bulk_load(smem_u32(sSFB + s * C::kSfbBytes + jb * kKBlocksPerStage * 512),
-                      p.sfb + (rb * p.ka + kt * kKBlocksPerStage) * 512, sf_bytes, db);
-          }
         }
       }
       if (!ok) {
+        // The leader's "full" counts both CTAs' bytes (and the scale writers, which may have
+        // left early: the bounded wait then gives the copies far longer than they take); the
+        // closing cluster barrier keeps the peer resident until it returns.
         for (int back = 1; back <= C::kStages && it - back >= 0; ++back) {
           const int f = it - back;
-          mbar_wait_drain(smem_u32(&sfd[f % C::kStages]), static_cast<uint32_t>(f / C::kStages) & 1u,
-                          p.err_word);
           if (rank == 0)
             mbar_wait_drain(smem_u32(&full[f % C::kStages]),
                             static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
@@ -760,37 +746,40 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     int it = 0;
     bool ok = true;
     for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      const int ra = tm * 2 + static_cast<int>(rank);  // 128-row blocks
+      const int rb0 = tn * 2;
       for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
         if ((it % kWriterGroups) != wgroup) continue;
         const int s = it % C::kStages;
         const int slot = it % C::kSfSlots;
-        // Keep "sfd" at most one phase ahead of this wait (the writer groups alternate stages):
-        // the stage's previous use must have been consumed first.
-        if (!mbar_wait_cluster(smem_u32(&empty[s]),
-                               (static_cast<uint32_t>(it / C::kStages) & 1u) ^ 1u, abort_flag,
-                               p.err_word, kErrWaitSfEmpty)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(smem_u32(&sfd[s]), static_cast<uint32_t>(it / C::kStages) & 1u, abort_flag,
-                       p.err_word, kErrWaitTmaFull)) {
-          ok = false;
-          break;
-        }
-        const uint8_t* sfa_s = sSFA + s * C::kSfaBytes + lane * 16;
-        const uint8_t* sfb_s = sSFB + s * C::kSfbBytes + lane * 16;
-        uint32_t va[16], vb[32];
+        int nkb = p.ka - kt * kKBlocksPerStage;
+        if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+        // This CTA's 128 rows of A (word q only: see the one-SM kernel) and all 256 rows of B,
+        // straight from global memory (L2).
+        uint32_t va[kKBlocksPerStage], vb[32];
 #pragma unroll
         for (int kb = 0; kb < kKBlocksPerStage; ++kb) {
-          const uint4 w = *reinterpret_cast<const uint4*>(sfa_s + kb * 512);
-          va[4 * kb + 0] = w.x; va[4 * kb + 1] = w.y; va[4 * kb + 2] = w.z; va[4 * kb + 3] = w.w;
+          va[kb] = 0u;
+          if (kb < nkb && ra < p.sfa_rowblocks)
+            va[kb] = __ldg(reinterpret_cast<const uint32_t*>(
+                p.sfa + (static_cast<size_t>(ra) * p.ka + kt * kKBlocksPerStage + kb) * 512 +
+                lane * 16 + q * 4));
 #pragma unroll
           for (int jb = 0; jb < 2; ++jb) {
-            const uint4 x = *reinterpret_cast<const uint4*>(sfb_s + jb * kKBlocksPerStage * 512 + kb * 512);
+            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            if (kb < nkb && rb0 + jb < p.sfb_rowblocks)
+              x = __ldg(reinterpret_cast<const uint4*>(
+                  p.sfb + (static_cast<size_t>(rb0 + jb) * p.ka + kt * kKBlocksPerStage + kb) * 512 +
+                  lane * 16));
             const int o = kb * 8 + 4 * jb;
             vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
           }
         }
+        // The slot's previous use (stage it - kSfSlots) must have been consumed; because
+        // kSfSlots <= kStages this also orders the arrival below after the leader's "full"
+        // barrier finished its previous phase.
         if (!mbar_wait_cluster(smem_u32(&sf_empty[slot]),
                                (static_cast<uint32_t>(it / C::kSfSlots) & 1u) ^ 1u, abort_flag,
                                p.err_word, kErrWaitSfEmpty)) {
@@ -799,7 +788,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         tc_fence_after();
         const uint32_t sf_t = lane_base + C::kSfCol + slot * kSfSlotCols;
-        tmem_st_32x32b_x16(sf_t, va);
+#pragma unroll
+        for (int kb = 0; kb < kKBlocksPerStage; ++kb) tmem_st_32x32b_x1(sf_t + kb * 4 + q, va[kb]);
         tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
         tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
         tc_wait_st();

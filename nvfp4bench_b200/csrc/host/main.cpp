@@ -277,29 +277,34 @@ void write_json(const std::string& path, const std::vector<BenchResult>& rows, c
   f << "  ]\n}\n";
 }
 
+// The tcgen05 FP4 ladder: zero operands (the issue-rate ceiling at full clock), then random
+// E2M1 operands timed alone (burst) and back to back for about a second (sustained, under the
+// power cap), each with the SM clock it ran at. Returns the random-data burst figure of the
+// one-SM N=256 rung, the roof a GEMM on real operands timed alone is held to.
 double run_ladder(const Dev& dev, bool print) {
   std::string err;
-  double best = 0;
-  for (int n : {128, 256}) {
-    double tf = 0;
-    if (!nvfp4b200::peak_ladder(n, dev.sms, 4096, 10, &tf, 0, &err)) {
+  double roof = 0;
+  struct Rung { int n, cg; uint32_t seed; int sustained; const char* what; };
+  const Rung rungs[] = {{128, 1, 0u, 0, "zero data, burst"},  {256, 1, 0u, 0, "zero data, burst"},
+                        {256, 2, 0u, 0, "zero data, burst"},  {256, 1, 0x5EEDu, 0, "random data, burst"},
+                        {256, 2, 0x5EEDu, 0, "random data, burst"},
+                        {256, 1, 0x5EEDu, 1, "random data, sustained ~1 s"},
+                        {256, 2, 0x5EEDu, 1, "random data, sustained ~1 s"}};
+  for (const Rung& r : rungs) {
+    const int units = r.cg == 2 ? dev.sms / 2 : dev.sms;
+    const nvfp4b200::PeakOptions o{r.n, r.cg, units, 4096, r.sustained ? 3000 : 10, r.seed, r.sustained};
+    double tf = 0, mhz = 0;
+    if (!nvfp4b200::peak_ladder_ex(o, &tf, &mhz, 0, &err)) {
       std::printf("peak ladder failed: %s\n", err.c_str());
-      return 0;
+      return roof;
     }
     if (print)
-      std::printf("tcgen05 kind::mxf4nvf4 block_scale M128 x N%d x K64, %d CTAs: %8.1f TFLOPS\n", n,
-                  dev.sms, tf);
-    best = std::max(best, tf);
+      std::printf("tcgen05 kind::mxf4nvf4 block_scale %s M%d x N%d x K64, %d %s, %s: %8.1f TFLOPS at %.0f MHz\n",
+                  r.cg == 2 ? "cta_group::2" : "cta_group::1", r.cg == 2 ? 256 : 128, r.n, units,
+                  r.cg == 2 ? "SM pairs" : "CTAs", r.what, tf, mhz);
+    if (r.cg == 1 && r.n == 256 && r.seed && !r.sustained) roof = tf;
   }
-  double tf2 = 0;
-  if (nvfp4b200::peak_ladder_pair(256, dev.sms / 2, 4096, 10, &tf2, 0, &err)) {
-    if (print)
-      std::printf("tcgen05 kind::mxf4nvf4 block_scale cta_group::2 M256 x N256 x K64, %d SM pairs: %8.1f TFLOPS\n",
-                  dev.sms / 2, tf2);
-  } else if (print) {
-    std::printf("pair rung failed: %s\n", err.c_str());
-  }
-  return best;
+  return roof;
 }
 
 void run_bandwidth() {

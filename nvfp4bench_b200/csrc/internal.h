@@ -52,6 +52,16 @@ bool naive_gemm_nt(const float* A, const float* B, int M, int N, int K, float* C
 // ---- roofs (roofs.cu) ----------------------------------------------------------------
 bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, size_t bytes,
                        int iters, double* gbs, cudaStream_t s, std::string* err);
+// One rung of the tcgen05 FP4 ladder. cta_group 1: `units` CTAs of M=128 x N=n MMAs; 2: `units`
+// SM pairs of M=256 x N=256. seed 0 stages zero operands, otherwise pseudo-random E2M1 bytes.
+// sustained 0: best of `reps` launches timed one by one; 1: mean of `reps` back-to-back launches.
+struct PeakOptions {
+  int n, cta_group, units, iters, reps;
+  uint32_t seed;
+  int sustained;
+};
+bool peak_ladder_ex(const PeakOptions& o, double* tflops, double* sm_mhz, cudaStream_t s,
+                    std::string* err);
 bool peak_ladder(int n, int ctas, int iters, int reps, double* tflops, cudaStream_t s,
                  std::string* err);
 // SM-pair rung: `clusters` clusters of 2 CTAs, cta_group::2 MMAs of M=256 x n x K=64.

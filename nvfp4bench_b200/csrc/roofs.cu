@@ -7,10 +7,13 @@
 //
 // Compute roof: replaces the reference's register-resident mma.sync ladder
 // (src/peak.cu:23-156, which cannot run on sm_100a) with a memory-free tcgen05 rung: each CTA
-// stages one zeroed A/B tile and its scales once, then one elected thread issues `iters`
+// stages one A/B tile and its scales once, then one elected thread issues `iters`
 // tcgen05.mma kind::mxf4nvf4 block_scale (M=128, N=n, K=64) back to back into one TMEM
-// accumulator and waits for their completion through tcgen05.commit. Throughput does not
-// depend on the data.
+// accumulator and waits for their completion through tcgen05.commit. The tile is zero or, with
+// a non-zero seed, pseudo-random E2M1 bytes: the issue rate does not depend on the data, but
+// the power drawn does, and under the 1 kW cap the SM clock (which the rung reports, from
+// clock64 against globaltimer on CTA 0) falls with it. The random-data rung, timed as the mean
+// of back-to-back launches, is the sustained FP4 roof for a GEMM on real operands.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -50,16 +53,40 @@ __global__ void triad_kernel(const float4* __restrict__ a, const float4* __restr
 
 constexpr int kPeakThreads = 128;
 
+__device__ unsigned long long g_peak_clk[2];  // CTA 0 of the last rung: SM cycles, ns
+
+// Fill `bytes` (a multiple of 16) of shared memory with zeros or seeded pseudo-random bytes.
+__device__ __forceinline__ void fill_tile(uint8_t* dst, int bytes, uint32_t seed) {
+  for (int i = threadIdx.x; i < bytes / 4; i += blockDim.x) {
+    uint32_t x = 0;
+    if (seed) {
+      x = (static_cast<uint32_t>(i) + blockIdx.x * 0x01000193u) * 0x9E3779B1u ^ seed;
+      x ^= x >> 16;
+      x *= 0x85EBCA6Bu;
+      x ^= x >> 13;
+      x *= 0xC2B2AE35u;
+      x ^= x >> 16;
+    }
+    reinterpret_cast<uint32_t*>(dst)[i] = x;
+  }
+}
+
+__device__ __forceinline__ void record_clock(long long c0, uint64_t n0) {
+  if (blockIdx.x == 0) {
+    g_peak_clk[0] = static_cast<unsigned long long>(clock64() - c0);
+    g_peak_clk[1] = globaltimer_ns() - n0;
+  }
+}
+
 template <int N>
-__global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32_t* err_word) {
+__global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32_t seed, uint32_t* err_word) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   constexpr int kA = 128 * 128, kB = N * 128, kSf = 4096;
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kA + kB + kSf);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  for (int i = threadIdx.x; i < (kA + kB + kSf) / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  fill_tile(smem, kA + kB, seed);
   // Unit scales (UE4M3 1.0 = 0x38) so the accumulator stays finite.
   for (int i = threadIdx.x; i < kSf; i += blockDim.x) smem[kA + kB + i] = 0x38;
   if (threadIdx.x == 0) {
@@ -83,10 +110,13 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32
     tc_cp_32x128b_x4(sfb_t + 4, make_sdesc(sf_s + 1024, 16, 128, 0));
     const uint32_t idesc = make_idesc_mxf4nvf4(128, N);
     const uint64_t ad = make_sdesc(a_s, 16, 1024, 2), bd = make_sdesc(b_s, 16, 1024, 2);
+    const long long c0 = clock64();
+    const uint64_t n0 = globaltimer_ns();
     for (int i = 0; i < iters; ++i) tc_mma_mxf4nvf4(tbase, ad, bd, idesc, sfa_t, sfb_t, i > 0);
     tc_commit(smem_u32(bar));
     volatile int never = 0;
     mbar_wait(smem_u32(bar), 0, &never, err_word, kErrWaitDrain);
+    record_clock(c0, n0);
   }
   tc_fence_before();
   __syncthreads();
@@ -97,15 +127,15 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32
 // SM-pair rung: clusters of two CTAs; the leader issues M=256 x N x K=64 MMAs with
 // cta_group::2 (each SM computes 128 x N), both CTAs allocate TMEM and hold scale copies.
 template <int N>
-__global__ void __launch_bounds__(kPeakThreads, 1) peak_pair_kernel(int iters, uint32_t* err_word) {
+__global__ void __launch_bounds__(kPeakThreads, 1) peak_pair_kernel(int iters, uint32_t seed, uint32_t* err_word) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   constexpr int kA = 128 * 128, kB = (N / 2) * 128, kSf = 4096;
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kA + kB + kSf);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  for (int i = threadIdx.x; i < (kA + kB) / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  fill_tile(smem, kA + kB, seed);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(bar), 1);
     fence_mbar_init();
@@ -136,11 +166,14 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_pair_kernel(int iters, u
     const uint32_t a_s = smem_u32(smem), b_s = smem_u32(smem + kA);
     const uint32_t idesc = make_idesc_mxf4nvf4(256, N);
     const uint64_t ad = make_sdesc(a_s, 16, 1024, 2), bd = make_sdesc(b_s, 16, 1024, 2);
+    const long long c0 = clock64();
+    const uint64_t n0 = globaltimer_ns();
     for (int i = 0; i < iters; ++i)
       tc_mma_mxf4nvf4_pair(tbase, ad, bd, idesc, tbase + 448, tbase + 452, i > 0);
     tc_commit_pair(smem_u32(bar));
     volatile int never = 0;
     mbar_wait(smem_u32(bar), 0, &never, err_word, kErrWaitDrain);
+    record_clock(c0, n0);
   }
   tc_fence_before();
   __syncthreads();
@@ -150,62 +183,6 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_pair_kernel(int iters, u
 }
 
 }  // namespace
-
-bool peak_ladder_pair(int n, int clusters, int iters, int reps, double* tflops, cudaStream_t s,
-                      std::string* err) {
-  if (n != 256 || clusters < 1 || iters < 1 || reps < 1 || !tflops) {
-    set_err(err, "peak (pair): n must be 256, clusters/iters/reps >= 1");
-    return false;
-  }
-  uint32_t* ew = device_error_word(err);
-  if (!ew) return false;
-  const int smem = 1024 + 128 * 128 + 128 * 128 + 4096 + 64;
-  cudaError_t e = cudaFuncSetAttribute(peak_pair_kernel<256>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) {
-    set_err(err, std::string("peak pair attr: ") + cudaGetErrorString(e));
-    return false;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(kPeakThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  auto launch = [&]() { return cudaLaunchKernelEx(&cfg, peak_pair_kernel<256>, iters, ew); };
-  if ((e = launch()) != cudaSuccess) {
-    set_err(err, std::string("peak pair launch: ") + cudaGetErrorString(e));
-    return false;
-  }
-  cudaEvent_t a, b;
-  cudaEventCreate(&a);
-  cudaEventCreate(&b);
-  float best = 1e30f;
-  for (int r = 0; r < reps; ++r) {
-    cudaEventRecord(a, s);
-    launch();
-    cudaEventRecord(b, s);
-    cudaEventSynchronize(b);
-    float ms = 0;
-    cudaEventElapsedTime(&ms, a, b);
-    best = std::min(best, ms);
-  }
-  cudaEventDestroy(a);
-  cudaEventDestroy(b);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_err(err, std::string("peak pair: ") + cudaGetErrorString(e));
-    return false;
-  }
-  *tflops = 2.0 * 256.0 * n * 64.0 * static_cast<double>(clusters) * iters / (best * 1e-3) / 1e12;
-  return true;
-}
 
 bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, size_t bytes,
                        int iters, double* gbs, cudaStream_t s, std::string* err) {
@@ -264,41 +241,66 @@ bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, s
   return true;
 }
 
-bool peak_ladder(int n, int ctas, int iters, int reps, double* tflops, cudaStream_t s,
-                 std::string* err) {
-  if ((n != 128 && n != 256) || ctas < 1 || iters < 1 || reps < 1 || !tflops) {
-    set_err(err, "peak: n must be 128 or 256, ctas/iters/reps >= 1");
+bool peak_ladder_ex(const PeakOptions& o, double* tflops, double* sm_mhz, cudaStream_t s,
+                    std::string* err) {
+  const bool pair = o.cta_group == 2;
+  if ((o.cta_group != 1 && !pair) || (pair ? o.n != 256 : (o.n != 128 && o.n != 256)) ||
+      o.units < 1 || o.iters < 1 || o.reps < 1 || !tflops) {
+    set_err(err, "peak: cta_group 1 (n 128 or 256) or 2 (n 256); units, iters, reps >= 1");
     return false;
   }
   uint32_t* ew = device_error_word(err);
   if (!ew) return false;
-  const int smem = 1024 + 128 * 128 + n * 128 + 4096 + 64;
-  cudaError_t e;
-  if (n == 256)
-    e = cudaFuncSetAttribute(peak_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  else
-    e = cudaFuncSetAttribute(peak_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int kb = pair ? o.n / 2 : o.n;
+  const int smem = 1024 + 128 * 128 + kb * 128 + 4096 + 64;
+  void (*kern)(int, uint32_t, uint32_t*) =
+      pair ? peak_pair_kernel<256> : (o.n == 256 ? peak_kernel<256> : peak_kernel<128>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_err(err, std::string("peak attr: ") + cudaGetErrorString(e));
     return false;
   }
-  auto launch = [&]() {
-    if (n == 256) peak_kernel<256><<<ctas, kPeakThreads, smem, s>>>(iters, ew);
-    else peak_kernel<128><<<ctas, kPeakThreads, smem, s>>>(iters, ew);
-  };
-  launch();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(pair ? 2 * o.units : o.units, 1, 1);
+  cfg.blockDim = dim3(kPeakThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = pair ? attr : nullptr;
+  cfg.numAttrs = pair ? 1 : 0;
+  const uint32_t seed = o.seed;
+  auto launch = [&]() { return cudaLaunchKernelEx(&cfg, kern, o.iters, seed, ew); };
+  if ((e = launch()) != cudaSuccess) {
+    set_err(err, std::string("peak launch: ") + cudaGetErrorString(e));
+    return false;
+  }
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
-  float best = 1e30f;
-  for (int r = 0; r < reps; ++r) {
+  float ms_used = 1e30f;
+  if (o.sustained) {
+    // Back-to-back launches between one pair of events: the mean, under the power cap.
     cudaEventRecord(a, s);
-    launch();
+    for (int r = 0; r < o.reps; ++r) launch();
     cudaEventRecord(b, s);
     cudaEventSynchronize(b);
     float ms = 0;
     cudaEventElapsedTime(&ms, a, b);
-    best = std::min(best, ms);
+    ms_used = ms / o.reps;
+  } else {
+    for (int r = 0; r < o.reps; ++r) {
+      cudaEventRecord(a, s);
+      launch();
+      cudaEventRecord(b, s);
+      cudaEventSynchronize(b);
+      float ms = 0;
+      cudaEventElapsedTime(&ms, a, b);
+      ms_used = std::min(ms_used, ms);
+    }
   }
   cudaEventDestroy(a);
   cudaEventDestroy(b);
@@ -307,9 +309,24 @@ bool peak_ladder(int n, int ctas, int iters, int reps, double* tflops, cudaStrea
     set_err(err, std::string("peak: ") + cudaGetErrorString(e));
     return false;
   }
-  const double flops = 2.0 * 128.0 * n * 64.0 * static_cast<double>(ctas) * iters;
-  *tflops = flops / (best * 1e-3) / 1e12;
+  const double m = pair ? 256.0 : 128.0;
+  *tflops = 2.0 * m * o.n * 64.0 * static_cast<double>(o.units) * o.iters / (ms_used * 1e-3) / 1e12;
+  if (sm_mhz) {
+    unsigned long long clk[2] = {0, 0};
+    cudaMemcpyFromSymbol(clk, g_peak_clk, sizeof(clk));
+    *sm_mhz = clk[1] ? 1e3 * static_cast<double>(clk[0]) / static_cast<double>(clk[1]) : 0.0;
+  }
   return true;
+}
+
+bool peak_ladder(int n, int ctas, int iters, int reps, double* tflops, cudaStream_t s,
+                 std::string* err) {
+  return peak_ladder_ex(PeakOptions{n, 1, ctas, iters, reps, 0u, 0}, tflops, nullptr, s, err);
+}
+
+bool peak_ladder_pair(int n, int clusters, int iters, int reps, double* tflops, cudaStream_t s,
+                      std::string* err) {
+  return peak_ladder_ex(PeakOptions{n, 2, clusters, iters, reps, 0u, 0}, tflops, nullptr, s, err);
 }
 
 }  // namespace nvfp4b200

@@ -28,3 +28,17 @@ def test_peak_ladder(api):
     tf = api.peak(256, 148, 2048, 3)
     assert tf > 1000  # TFLOP/s; dense FP4 nominal is about 9000 at boost clock
     assert api.device_error() == 0
+
+
+@pytest.mark.parametrize("cta_group", [1, 2])
+def test_peak_ladder_random_data_and_clock(api, cta_group):
+    units = 148 if cta_group == 1 else 74
+    tf, mhz = api.peak_ex(256, cta_group, units, 2048, 3, seed=0x5EED)
+    assert tf > 1000 and 300 < mhz < 2200
+    tf_s, mhz_s = api.peak_ex(256, cta_group, units, 2048, 20, seed=0x5EED, sustained=True)
+    assert tf_s > 1000 and 300 < mhz_s < 2200
+    # Same issue rate per cycle whatever the data: TF/s per MHz agree within 15%.
+    assert abs(tf / mhz - tf_s / mhz_s) / (tf / mhz) < 0.15
+    with pytest.raises(api.Nvfp4Error):
+        api.peak_ex(128, 2, units, 16, 1)
+    assert api.device_error() == 0
