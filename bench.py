@@ -208,15 +208,48 @@ def run_b200(args, rank, world, local_rank):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
-    # Measured compute roof for this run (tcgen05 FP4 ladder).
-    peak_tf = None if args.kernel_only else api.peak(
-        256, torch.cuda.get_device_properties(dev).multi_processor_count, 4096, 5)
+    # Measured compute roofs for this run (tcgen05 FP4 ladder, M128 N256 K64 on every SM):
+    # random E2M1 operands timed alone (the roof for this GEMM, which is timed alone), zero
+    # operands (the issue-rate ceiling at full clock) and random operands back to back for
+    # about a second (under the power cap); each with the SM clock it ran at.
+    ladder = {}
+    if not args.kernel_only:
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        for key, seed, sustained, reps in (("random_burst", 0x5EED, False, 5),
+                                           ("zero_burst", 0, False, 5),
+                                           ("random_sustained", 0x5EED, True, 2000)):
+            tf, mhz = api.peak_ex(256, 1, sms, 4096, reps, seed=seed, sustained=sustained)
+            ladder[key] = {"tflops": round(tf, 1), "sm_mhz": round(mhz)}
+    peak_tf = ladder["random_burst"]["tflops"] if ladder else None
+
+    # Decode shapes (M <= 128) stream the weight once per step, and a flush that writes 256 MiB
+    # leaves L2 full of dirty lines whose write-back competes with that stream. They use inputs
+    # larger than L2 instead: the weight is rotated over R copies holding at least 3x L2, so
+    # each step reads a weight that the steps since its last use have evicted.
+    decode = M <= 128
+    rot = [gargs]
+    if decode:
+        wbytes = B.packed.numel() + B.scales_tc.numel()
+        copies = max(2, -(-3 * 126_000_000 // wbytes))
+        keep = []
+        for _ in range(copies - 1):
+            bp, bs = B.packed.clone(), B.scales_tc.clone()
+            keep.append((bp, bs))
+            rot.append(api.gemm_args(A.packed, A.scales_tc, bp, bs, M, N, K, C,
+                                     sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
+                                     cta_group=args.cta_group))
+    step_no = [0]
 
     def step():
-        api.launch(gargs)
+        api.launch(rot[step_no[0] % len(rot)])
+        step_no[0] += 1
 
-    for _ in range(max(3, args.warmup)):
-        flush.zero_()
+    def before_step():
+        if not decode:
+            flush.zero_()
+
+    for _ in range(max(3, args.warmup, 2 * len(rot) if decode else 0)):
+        before_step()
         step()
     torch.cuda.synchronize()
     if world > 1:
@@ -231,16 +264,31 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    for i in range(args.steps):
-        flush.zero_()
-        starts[i].record(stream)
-        step()
-        ends[i].record(stream)
+    if decode:
+        # A decode step is shorter than the host's launch path: a GPU spin in front lets the
+        # host enqueue every step first, so the events time the device, not the launches.
+        torch.cuda._sleep(args.steps * 100_000)
+    if decode:
+        # One event pair around the K back-to-back steps: an event between two launches
+        # would stand between them and stop the next one's set-up from overlapping.
+        starts[0].record(stream)
+        for i in range(args.steps):
+            step()
+        ends[0].record(stream)
+    else:
+        for i in range(args.steps):
+            before_step()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop() if clocks else None
-    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if decode:
+        times = [starts[0].elapsed_time(ends[0]) / args.steps] * args.steps
+    else:
+        times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     mean_ms = sum(times) / len(times)
     min_ms, med_ms = min(times), statistics.median(times)
     mean_ms, min_ms, med_ms = max_over_ranks([mean_ms, min_ms, med_ms], device=dev)
@@ -262,6 +310,8 @@ def run_b200(args, rank, world, local_rank):
     # sustained=median of 50.
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(50)]
+    if decode:
+        torch.cuda._sleep(len(ev) * 100_000)
     for s_, e_ in ev:
         s_.record(stream)
         step()
@@ -330,12 +380,14 @@ def run_b200(args, rank, world, local_rank):
                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs")
                     else "fallback 6650 GB/s",
                     "traffic": traffic, "algorithmic_bytes": abytes,
-                    "tcgen05_fp4_ladder_tflops": peak_tf}
+                    "tcgen05_fp4_ladder": ladder}
     else:
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf,
                     "unit": "TFLOP/s", "frac": achieved / peak_tf,
                     "peak_source": "tcgen05 kind::mxf4nvf4 ladder measured in this run "
-                                   "(M128 N256 K64, 148 CTAs)",
+                                   "(M128 N256 K64 on every SM, random E2M1 operands, best "
+                                   "of 5 single launches)",
+                    "tcgen05_fp4_ladder": ladder,
                     "bf16_measured_peak": peaks.get("bf16_tflops"),
                     "traffic": traffic, "algorithmic_bytes": abytes}
     cpu = None
@@ -351,7 +403,11 @@ def run_b200(args, rank, world, local_rank):
         "data": "synthetic N(0,1), seeded, quantised on the GPU",
         "config": {"workload": desc, "M": M, "N_per_gpu": N, "K": K, "out": od,
                    "parallelism": f"N-sharded x{world}" if world > 1 else "single GPU",
-                   "l2": "flushed (256 MiB write) before every step; per-step CUDA events",
+                   "l2": (f"weight rotated over {len(rot)} copies ({len(rot)} x "
+                          f"{(B.packed.numel() + B.scales_tc.numel()) / 1e6:.1f} MB > 3x L2), "
+                          "no flush; host enqueue ahead of a GPU spin; per-step CUDA events"
+                          if decode else
+                          "flushed (256 MiB write) before every step; per-step CUDA events"),
                    "tile_n": args.tile_n or "auto", "sf_layout": "tcgen05"},
         "burst_tflops": burst_tf, "sustained_tflops": sust_tf,
         "roofline": roofline,

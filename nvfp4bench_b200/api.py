@@ -80,6 +80,8 @@ def lib():
         L.nvfp4_b200_measure_bandwidth.argtypes = [ip, vp, vp, vp, sz, ip,
                                                    C.POINTER(C.c_double), vp, *errs]
         L.nvfp4_b200_peak.argtypes = [ip, ip, ip, ip, C.POINTER(C.c_double), vp, *errs]
+        L.nvfp4_b200_peak_ex.argtypes = [ip, ip, ip, ip, ip, C.c_uint32, ip, C.POINTER(C.c_double),
+                                         C.POINTER(C.c_double), vp, *errs]
         L.nvfp4_b200_device_error.argtypes = [ip, C.POINTER(C.c_uint32), *errs]
         L.nvfp4_b200_wait_selftest.argtypes = [C.c_uint64, C.POINTER(C.c_uint32), *errs]
         L.nvfp4_b200_version.restype = C.c_char_p
@@ -93,17 +95,19 @@ def lib():
 
 def _call(fn, *args):
     buf = C.create_string_buffer(512)
-    rc = fn(*args, buf, len(buf))
+    rc = fn(*args, buf, C.c_size_t(len(buf)))
     if rc != 0:
         raise Nvfp4Error(rc, buf.value.decode(errors="replace"))
 
 
-def _stream(stream) -> Optional[int]:
+def _stream(stream) -> C.c_void_p:
+    # A typed pointer: a bare Python int is passed as a 32-bit value, which in a stack-passed
+    # argument slot leaves the upper half of the 64-bit handle undefined.
     if stream is None:
-        return torch.cuda.current_stream().cuda_stream
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
     if isinstance(stream, torch.cuda.Stream):
-        return stream.cuda_stream
-    return int(stream)
+        return C.c_void_p(stream.cuda_stream)
+    return C.c_void_p(int(stream))
 
 
 def _ptr(t: Optional[torch.Tensor]):

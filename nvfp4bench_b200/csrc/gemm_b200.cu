@@ -1150,11 +1150,11 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
                    void* out, cudaStream_t s, std::string* err) {
   DeviceState* ds = device_state(err);
   if (!ds) return false;
-  // Few tokens and few 128-row weight tiles (e.g. M=16 x a 4096-row weight): the split-K
-  // weight-streaming kernel keeps every SM loading; measured slower than the general kernel
-  // once the weight alone has enough tiles to occupy half the SMs. An explicit tile shape or
-  // SM grouping selects the general kernel.
-  if (op.M <= 32 && (op.N + 127) / 128 < ds->sms / 2 && op.cta_group == 0 && op.tile_n == 0)
+  // At most one 128-row block of tokens (decode): the weight-streaming kernel (weight rows on
+  // the MMA's 128-row side, one CTA per SM, split-K over a cluster when the weight has fewer
+  // 128-row tiles than there are SMs). An explicit tile shape or SM grouping selects the
+  // general kernel.
+  if (op.M <= 128 && op.cta_group == 0 && op.tile_n == 0)
     return gemm_decode(op, sfa, sfb, out, s, err);
   int bn = op.tile_n;
   const int tiles_m = (op.M + kBM - 1) / kBM;

@@ -1,22 +1,29 @@
 // gemm_decode.cu - weight-streaming NVFP4 GEMM for decode shapes (M <= 128 tokens).
 //
-// BASELINE's decode configurations (M in {16, 64, 128} tokens x a 14336 x 4096 or 4096 x
-// 14336 weight) are HBM-bound: the weight B is read once and everything else is small. The
-// general kernel tiles M by 128 rows, so at M = 16 it keeps at most N/128 CTAs busy and runs
-// the MMA at 1/8 occupancy of its M; this kernel turns the problem around:
+// The decode configurations (M in {16, 64, 128} tokens x a 14336 x 4096 or 4096 x 14336
+// weight) are HBM-bound: the weight B is read once and everything else is small. The general
+// kernel tiles M by 128 rows, so at M = 16 it keeps at most N/256 CTAs busy and runs the MMA
+// at 1/8 of its M; this kernel turns the problem around:
 //   * the weight rows are the MMA's 128-row "A" side (D^T = B * A^T in TMEM, lane = weight
 //     row n), the tokens its "B" side with N = M rounded up to 16..128;
-//   * K is split over `splits` CTAs per 128-row weight tile so that about two CTAs per SM
-//     stream weights (small shared memory, 256 TMEM columns, 2 CTAs per SM);
-//   * partial sums go to an FP32 workspace; the last CTA of each tile (an atomic counter that
-//     it resets) adds them in split order - deterministic - and writes C. With one split the
-//     epilogue writes C directly.
+//   * one CTA per SM, each streaming its share of the weight through a deep ring of shared
+//     memory stages (6 to 10, about 190 KB in flight per SM);
+//   * when there are fewer 128-row weight tiles than SMs, the K range of a tile is split over
+//     the S CTAs of one thread-block cluster (S = 2, 4 or 8). Each CTA parks its FP32 partial
+//     sums in its own shared memory, and after a cluster barrier CTA r adds up its share of
+//     the tokens from all S partials through distributed shared memory, in rank order
+//     (deterministic), and stores C. No workspace, no atomics, no second pass.
 // The epilogue needs no transpose: thread = weight row n holds the values of all tokens, so a
 // warp stores 32 consecutive columns of C per token.
 //
-// Roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2..5 epilogue, warps
-// 6..9 scale writers (tcgen05.st of each stage's scales into its TMEM slot, as in the general
-// kernel). Bounded waits as everywhere (ptx.cuh).
+// Roles (320 threads): warp 0 producer (per stage: the weight and token tiles by TMA onto
+// "full", the stage's weight and token scale atoms by bulk copy onto "sfd"), warp 1 MMA
+// issuer, warps 2..5 epilogue, warps 6..9 scale writers. The writers move each stage's scales
+// from shared memory into a ring of three TMEM scale slots: weight scales (the MMA's A side,
+// rows = TMEM lanes) one column per quadrant, the one its MMA rows read; token scales (B
+// side) whole in every quadrant. (Loading them from global memory in the writers themselves
+// put an L2 round trip per stage on the critical path: one writer group, one stage at a
+// time.) Bounded waits as everywhere (ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -33,16 +40,16 @@ namespace nvfp4b200 {
 namespace {
 
 constexpr int kDThreads = 320;
-constexpr int kDMaxStages = 4;
-constexpr int kDTmemCols = 256;   // accumulator [0, 128) + up to 4 stage slots of 32 columns
+constexpr int kDTmemCols = 512;   // accumulator [0, 128) + kDSfSlots slots of 32 columns
 constexpr int kDSlotCols = 32;    // weight scales at +0 (4 per K-block), token scales at +16
+constexpr int kDSfSlots = 12;     // deep enough that the writer/MMA slot ring never throttles
+constexpr int kDMaxCluster = 8;
+constexpr int kDSmemBudget = 200 * 1024;
 
 struct DParams {
-  const uint8_t* sfw;   // weight (B operand) scales, tcgen05 layout over N rows
-  const uint8_t* sft;   // token (A operand) scales, tcgen05 layout over M rows
+  const uint8_t* sfw;   // weight (MMA A side) scales, tcgen05 layout over N rows
+  const uint8_t* sft;   // token (MMA B side) scales, tcgen05 layout over M rows
   void* out;
-  float* ws;            // [splits][tiles_n][mpad][128] partial sums (splits > 1)
-  int* counters;        // [tiles_n], zero between calls
   int M, N, K;
   float alpha;
   int out_bf16;
@@ -52,15 +59,19 @@ struct DParams {
 
 template <int MPAD>
 struct DCfg {
-  // Stages: 4, or 3 for 64-token tiles so that two CTAs still fit one SM's shared memory.
-  static constexpr int kStages = MPAD == 64 ? 3 : kDMaxStages;
   static constexpr int kWBytes = 128 * 128;           // 128 weight rows x 256 FP4
   static constexpr int kTBytes = MPAD * 128;          // MPAD token rows x 256 FP4
   static constexpr int kSfBytes = 4 * 512;            // one 128-row atom per K-block
   static constexpr int kStageBytes = kWBytes + kTBytes + 2 * kSfBytes;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
-  static constexpr int kMinBlocks = MPAD <= 64 ? 2 : 1;
-  static_assert(kStages * kDSlotCols + 128 <= kDTmemCols, "TMEM budget");
+  static constexpr int kStages0 = kDSmemBudget / kStageBytes;
+  static constexpr int kStages = kStages0 > 10 ? 10 : kStages0;
+  static constexpr int kPartBytes = MPAD * 128 * 4;   // FP32 partial sums, [token][row]
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
+  static_assert(kPartBytes <= kStages * kStageBytes, "partials reuse the stage memory");
+  // A writer's slot wait (the MMA of stage i - slots finished) must also order its "full"
+  // arrival after that barrier's previous phase (stage i - stages): slots <= stages.
+  static constexpr int kSlots = kDSfSlots < kStages ? kDSfSlots : kStages;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ void store_out(const DParams& p, int m, int n, float v) {
@@ -70,8 +81,17 @@ __device__ __forceinline__ void store_out(const DParams& p, int m, int n, float 
     reinterpret_cast<float*>(p.out)[static_cast<size_t>(m) * p.N + n] = v;
 }
 
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
 template <int MPAD>
-__global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
+__global__ void __launch_bounds__(kDThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
                        const __grid_constant__ CUtensorMap tmap_t, const DParams p) {
   using C = DCfg<MPAD>;
@@ -82,17 +102,20 @@ __global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
   uint8_t* sT = sW + C::kStages * C::kWBytes;
   uint8_t* sSFW = sT + C::kStages * C::kTBytes;
   uint8_t* sSFT = sSFW + C::kStages * C::kSfBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFT + C::kStages * C::kSfBytes);
-  uint64_t* full = bars;                 // operand bytes + producer + 4 scale writers
-  uint64_t* empty = full + C::kStages;     // stage (smem and scale slot) consumed
-  uint64_t* sfd = empty + C::kStages;      // scale bytes landed
-  uint64_t* acc_full = sfd + C::kStages;
+  float* part = reinterpret_cast<float*>(smem);  // after the last MMA: [MPAD][128] partials
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = bars;                      // operand bytes + producer + 4 scale writers
+  uint64_t* empty = full + C::kStages;        // smem stage consumed
+  uint64_t* sfd = empty + C::kStages;         // the stage's scale atoms landed
+  uint64_t* sf_empty = sfd + C::kStages;      // TMEM scale slot consumed
+  uint64_t* acc_full = sf_empty + C::kSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* last_flag = const_cast<int*>(abort_flag) + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tn = blockIdx.x % p.tiles_n, ks = blockIdx.x / p.tiles_n;
+  // Cluster = the K splits of one weight tile (cluster dims (splits, 1, 1)).
+  const int ks = static_cast<int>(blockIdx.x) % p.splits;
+  const int tn = static_cast<int>(blockIdx.x) / p.splits;
   const int kt0 = static_cast<int>(static_cast<long>(ks) * p.num_kt / p.splits);
   const int kt1 = static_cast<int>(static_cast<long>(ks + 1) * p.num_kt / p.splits);
 
@@ -102,9 +125,9 @@ __global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
       mbar_init(smem_u32(&empty[s]), 1);
       mbar_init(smem_u32(&sfd[s]), 1);
     }
+    for (int j = 0; j < C::kSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
     mbar_init(smem_u32(acc_full), 1);
     *abort_flag = 0;
-    *last_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_t);
@@ -117,8 +140,13 @@ __global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization: the set-up above overlaps the previous
+  // kernel on the stream; every global read and write comes after it has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       bool ok = true;
       int i = 0;
@@ -145,21 +173,27 @@ __global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
         tma_load_2d(smem_u32(sT + s * C::kTBytes), &tmap_t, kt * 128, 0, fb);
       }
       if (!ok) {
+        // The most recent fill of every stage lands before the CTA exits ("full" also counts
+        // the writers, which may have left early: the bounded wait then outlasts the copy).
         for (int back = 1; back <= C::kStages && i - back >= 0; ++back) {
           const int f = i - back;
           volatile int never = 0;
           mbar_wait(smem_u32(&sfd[f % C::kStages]), static_cast<uint32_t>(f / C::kStages) & 1u,
                     &never, p.err_word, kErrWaitDrain);
+          mbar_wait(smem_u32(&full[f % C::kStages]), static_cast<uint32_t>(f / C::kStages) & 1u,
+                    &never, p.err_word, kErrWaitDrain);
         }
       }
     }
   } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc_mxf4nvf4(128, MPAD);
       bool ok = true, issued = false;
       int i = 0;
       for (int kt = kt0; kt < kt1; ++kt, ++i) {
         const int s = i % C::kStages;
+        const int slot = i % C::kSlots;
         const uint32_t j = static_cast<uint32_t>(i / C::kStages);
         if (!mbar_spin_wait<false>(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word,
                                    kErrWaitTmaFull)) {
@@ -171,43 +205,50 @@ __global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
         if (nkb > 4) nkb = 4;
         const uint64_t ad0 = make_sdesc(smem_u32(sW + s * C::kWBytes), 16, 1024, 2);
         const uint64_t bd0 = make_sdesc(smem_u32(sT + s * C::kTBytes), 16, 1024, 2);
-        const uint32_t sf_t = tmem_base + 128 + s * kDSlotCols;
+        const uint32_t sf_t = tmem_base + 128 + slot * kDSlotCols;
         for (int kb = 0; kb < nkb; ++kb)
           tc_mma_mxf4nvf4(tmem_base, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
                           sf_t + 16 + kb * 4, (i > 0 || kb > 0) ? 1u : 0u);
         issued = true;
+        tc_commit(smem_u32(&sf_empty[slot]));
         tc_commit(smem_u32(&empty[s]));
       }
-      if (ok) {
-        tc_commit(smem_u32(acc_full));
-      } else if (issued) {
-        tc_commit(smem_u32(acc_full));
+      // acc_full also tells the epilogue that every MMA has finished reading shared memory.
+      if (ok || issued) tc_commit(smem_u32(acc_full));
+      if (!ok && issued) {
         volatile int never = 0;
         mbar_wait(smem_u32(acc_full), 0, &never, p.err_word, kErrWaitDrain);
       }
     }
   } else if (warp >= 6) {
-    // Scale writers: weight atom -> slot +0, token atom -> slot +16 (4 words per K-block).
+    // ---------------------------------------------------------------- scale writers
     const int q = warp & 3;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     int i = 0;
     for (int kt = kt0; kt < kt1; ++kt, ++i) {
       const int s = i % C::kStages;
+      const int slot = i % C::kSlots;
       const uint32_t j = static_cast<uint32_t>(i / C::kStages);
+      // One writer group takes every stage in order, so "sfd" is never two phases ahead.
       if (!mbar_wait(smem_u32(&sfd[s]), j & 1u, abort_flag, p.err_word, kErrWaitTmaFull)) break;
-      uint32_t vw[16], vt[16];
+      // Weight rows are TMEM lanes: quadrant q's MMA rows read only word q of each atom row.
+      // Token rows map to accumulator columns, read by every quadrant: all four words. Atoms
+      // past the end of K hold stale bytes that no MMA reads.
+      uint32_t vw[4], vt[16];
 #pragma unroll
       for (int kb = 0; kb < 4; ++kb) {
-        const uint4 w = *reinterpret_cast<const uint4*>(sSFW + s * C::kSfBytes + kb * 512 + lane * 16);
+        vw[kb] = *reinterpret_cast<const uint32_t*>(sSFW + s * C::kSfBytes + kb * 512 + lane * 16 + q * 4);
         const uint4 t = *reinterpret_cast<const uint4*>(sSFT + s * C::kSfBytes + kb * 512 + lane * 16);
-        vw[4 * kb] = w.x; vw[4 * kb + 1] = w.y; vw[4 * kb + 2] = w.z; vw[4 * kb + 3] = w.w;
         vt[4 * kb] = t.x; vt[4 * kb + 1] = t.y; vt[4 * kb + 2] = t.z; vt[4 * kb + 3] = t.w;
       }
-      if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word, kErrWaitSfEmpty))
+      if (!mbar_wait(smem_u32(&sf_empty[slot]),
+                     (static_cast<uint32_t>(i / C::kSlots) & 1u) ^ 1u, abort_flag, p.err_word,
+                     kErrWaitSfEmpty))
         break;
       tc_fence_after();
-      const uint32_t sf_t = lane_base + 128 + s * kDSlotCols;
-      tmem_st_32x32b_x16(sf_t, vw);
+      const uint32_t sf_t = lane_base + 128 + slot * kDSlotCols;
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) tmem_st_32x32b_x1(sf_t + kb * 4 + q, vw[kb]);
       tmem_st_32x32b_x16(sf_t + 16, vt);
       tc_wait_st();
       tc_fence_before();
@@ -215,43 +256,31 @@ __global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
       if (lane == 0) mbar_arrive(smem_u32(&full[s]));
     }
   } else {
-    // Epilogue: thread = weight row n (TMEM lane), registers = tokens.
+    // ---------------------------------------------------------------- epilogue
+    // Thread = weight row n (TMEM lane), registers = tokens.
     const int q = warp & 3;
     const int n_local = q * 32 + lane;
     const int n = tn * 128 + n_local;
-    bool ok = mbar_wait(smem_u32(acc_full), 0, abort_flag, p.err_word, kErrWaitAccFull);
+    const bool ok = mbar_wait(smem_u32(acc_full), 0, abort_flag, p.err_word, kErrWaitAccFull);
     tc_fence_after();
     const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    if (p.splits == 1) {
 #pragma unroll
-      for (int c0 = 0; c0 < MPAD; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(acc_t + c0, r);
-        tc_wait_ld();
+    for (int c0 = 0; c0 < MPAD; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(acc_t + c0, r);
+      tc_wait_ld();
+      if (p.splits == 1) {
         if (ok && n < p.N) {
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj)
-            if (c0 + jj < p.M) store_out(p, c0 + jj, n, __uint_as_float(r[jj]) * p.alpha);
+            if (c0 + jj < MPAD && c0 + jj < p.M)
+              store_out(p, c0 + jj, n, __uint_as_float(r[jj]) * p.alpha);
         }
-      }
-    } else {
-      float* part = p.ws + (static_cast<size_t>(ks) * p.tiles_n + tn) * MPAD * 128;
-#pragma unroll
-      for (int c0 = 0; c0 < MPAD; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(acc_t + c0, r);
-        tc_wait_ld();
+      } else {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj)
-          if (c0 + jj < MPAD) __stcg(part + (c0 + jj) * 128 + n_local, __uint_as_float(r[jj]));
+          if (c0 + jj < MPAD) part[(c0 + jj) * 128 + n_local] = __uint_as_float(r[jj]);
       }
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (q == (2 & 3) && lane == 0) {
-        const int old = atomicAdd(&p.counters[tn], 1);
-        *last_flag = (old == p.splits - 1) ? 1 : 0;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
     }
   }
 
@@ -260,49 +289,98 @@ __global__ void __launch_bounds__(kDThreads, DCfg<MPAD>::kMinBlocks)
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kDTmemCols);
 
-  if (p.splits > 1 && *last_flag) {
-    // The last CTA of this weight tile adds the splits' partial sums in split order. All 320
-    // threads take (token, row) pairs in turn; each pair's loads are independent of the
-    // stores (restrict) and issue together.
-    __threadfence();
-    const float* __restrict__ ws = p.ws + static_cast<size_t>(tn) * MPAD * 128;
-    const size_t split_stride = static_cast<size_t>(p.tiles_n) * MPAD * 128;
-    const int total = p.M * 128;
-    for (int idx = threadIdx.x; idx < total; idx += kDThreads) {
-      float acc = 0.0f;
-      for (int k2 = 0; k2 < p.splits; ++k2) acc += __ldcg(ws + k2 * split_stride + idx);
-      const int m = idx >> 7, nn = tn * 128 + (idx & 127);
-      if (nn < p.N) store_out(p, m, nn, acc * p.alpha);
+  if (p.splits > 1) {
+    // Every CTA of the cluster has its partials in shared memory after this barrier.
+    cluster_sync();
+    // CTA ks reduces tokens [m0, m1) over the cluster, in rank order.
+    const int per = (MPAD + p.splits - 1) / p.splits;
+    const int m0 = ks * per;
+    int m1 = m0 + per;
+    if (m1 > p.M) m1 = p.M;
+    const uint32_t part_s = smem_u32(part);
+    uint32_t peer[kDMaxCluster];
+#pragma unroll
+    for (int r = 0; r < kDMaxCluster; ++r)
+      peer[r] = r < p.splits ? mapa_shared(part_s, static_cast<uint32_t>(r)) : 0u;
+    if (*abort_flag == 0) {
+      // float4 units: 32 per token row of 128 weight rows.
+      for (int idx = m0 * 32 + static_cast<int>(threadIdx.x); idx < m1 * 32; idx += kDThreads) {
+        float4 v[kDMaxCluster];
+#pragma unroll
+        for (int r = 0; r < kDMaxCluster; ++r)
+          if (r < p.splits) v[r] = ld_dsmem_f32x4(peer[r] + static_cast<uint32_t>(idx) * 16u);
+        float4 acc = v[0];
+#pragma unroll
+        for (int r = 1; r < kDMaxCluster; ++r)
+          if (r < p.splits) {
+            acc.x += v[r].x; acc.y += v[r].y; acc.z += v[r].z; acc.w += v[r].w;
+          }
+        const int m = idx >> 5, nn = tn * 128 + (idx & 31) * 4;
+        const float o[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (nn + u < p.N) store_out(p, m, nn + u, o[u] * p.alpha);
+      }
     }
-    if (threadIdx.x == 0) p.counters[tn] = 0;
+    // No CTA leaves while a peer may still read its shared memory.
+    cluster_sync();
   }
 }
 
-struct DecodeWs {
-  float* ws = nullptr;
-  size_t ws_bytes = 0;
-  int* counters = nullptr;
-  int n_counters = 0;
+struct DecodeState {
   bool attr[4] = {false, false, false, false};
 };
 std::mutex g_dmu;
-std::vector<DecodeWs> g_dws;
+std::vector<DecodeState> g_dstate;
 
 template <int MPAD>
-bool launch_decode(const CUtensorMap& tw, const CUtensorMap& tt, const DParams& p, DecodeWs& w,
-                   int idx, cudaStream_t s, std::string* err) {
+bool launch_decode(const CUtensorMap& tw, const CUtensorMap& tt, DParams p, int sms,
+                   DecodeState& st, int idx, cudaStream_t s, std::string* err) {
   using C = DCfg<MPAD>;
-  if (!w.attr[idx]) {
+  if (!st.attr[idx]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_decode_kernel<MPAD>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_decode_kernel<MPAD>,
+                               cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) {
       set_err(err, std::string("cudaFuncSetAttribute (decode): ") + cudaGetErrorString(e));
       return false;
     }
-    w.attr[idx] = true;
+    st.attr[idx] = true;
   }
-  gemm_decode_kernel<MPAD><<<p.tiles_n * p.splits, kDThreads, C::kSmemBytes, s>>>(tw, tt, p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kDThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Split K over a cluster only while the clusters of all tiles are co-resident (one CTA
+  // per SM): splits = the largest power of two <= 8 with tiles * splits <= SMs, that the
+  // K range can feed and that the device can schedule.
+  int splits = 1;
+  while (splits * 2 <= kDMaxCluster && p.tiles_n * splits * 2 <= sms && splits * 2 <= p.num_kt)
+    splits *= 2;
+  for (; splits > 1; splits /= 2) {
+    attr[0].val.clusterDim.x = splits;
+    cfg.gridDim = dim3(p.tiles_n * splits, 1, 1);
+    int ncl = 0;
+    if (cudaOccupancyMaxActiveClusters(&ncl, gemm_decode_kernel<MPAD>, &cfg) == cudaSuccess &&
+        ncl >= p.tiles_n)
+      break;
+    cudaGetLastError();
+  }
+  p.splits = splits;
+  attr[0].val.clusterDim.x = splits;
+  cfg.gridDim = dim3(p.tiles_n * splits, 1, 1);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_decode_kernel<MPAD>, tw, tt, p);
   if (e != cudaSuccess) {
     set_err(err, std::string("decode launch: ") + cudaGetErrorString(e));
     return false;
@@ -335,52 +413,23 @@ bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_
   p.tiles_n = (op.N + 127) / 128;
   p.num_kt = (op.K + 255) / 256;
   p.ka = (op.K + 63) / 64;
-  const int per_sm = mpad <= 64 ? 2 : 1;
-  // One wave: as many K splits as keep tiles_n * splits within the co-resident CTA count.
-  int splits = (per_sm * sms) / p.tiles_n;
-  if (splits > p.num_kt) splits = p.num_kt;
-  if (splits < 1) splits = 1;
-  p.splits = splits;
+  p.splits = 1;
   p.err_word = device_error_word(err);
   if (!p.err_word) return false;
+  DecodeState* st = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_dmu);
-    if (static_cast<int>(g_dws.size()) <= dev) g_dws.resize(dev + 1);
-    DecodeWs& w = g_dws[dev];
-    const size_t need = static_cast<size_t>(splits) * p.tiles_n * mpad * 128 * sizeof(float);
-    if (splits > 1 && w.ws_bytes < need) {
-      if (w.ws) cudaFree(w.ws);
-      w.ws = nullptr;
-      w.ws_bytes = 0;
-      if (cudaMalloc(&w.ws, need) != cudaSuccess) {
-        set_err(err, "cudaMalloc of the decode workspace failed");
-        return false;
-      }
-      w.ws_bytes = need;
-    }
-    if (w.n_counters < p.tiles_n) {
-      if (w.counters) cudaFree(w.counters);
-      w.counters = nullptr;
-      w.n_counters = 0;
-      if (cudaMalloc(&w.counters, sizeof(int) * p.tiles_n) != cudaSuccess ||
-          cudaMemset(w.counters, 0, sizeof(int) * p.tiles_n) != cudaSuccess) {
-        set_err(err, "cudaMalloc of the decode counters failed");
-        return false;
-      }
-      w.n_counters = p.tiles_n;
-    }
-    p.ws = w.ws;
-    p.counters = w.counters;
+    if (static_cast<int>(g_dstate.size()) <= dev) g_dstate.resize(dev + 1);
+    st = &g_dstate[dev];
   }
   CUtensorMap tw, tt;
   if (!operand_map(&tw, op.b_packed, op.N, op.K, 128, err)) return false;
   if (!operand_map(&tt, op.a_packed, op.M, op.K, mpad, err)) return false;
-  DecodeWs& w = g_dws[dev];
   switch (mpad) {
-    case 16: return launch_decode<16>(tw, tt, p, w, 0, s, err);
-    case 32: return launch_decode<32>(tw, tt, p, w, 1, s, err);
-    case 64: return launch_decode<64>(tw, tt, p, w, 2, s, err);
-    default: return launch_decode<128>(tw, tt, p, w, 3, s, err);
+    case 16: return launch_decode<16>(tw, tt, p, sms, *st, 0, s, err);
+    case 32: return launch_decode<32>(tw, tt, p, sms, *st, 1, s, err);
+    case 64: return launch_decode<64>(tw, tt, p, sms, *st, 2, s, err);
+    default: return launch_decode<128>(tw, tt, p, sms, *st, 3, s, err);
   }
 }
 

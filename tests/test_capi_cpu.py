@@ -64,3 +64,15 @@ def test_reference_backend_slots_report_not_built():
     text = open(os.path.join(ROOT, "include", "gemm.h")).read()
     for k in ("Stub", "Cutlass", "Custom", "B200"):
         assert f"KernelKind::{k}" in text
+
+
+def test_every_export_declares_argtypes():
+    """Each entry point with arguments has ctypes argtypes (an untyped 64-bit argument that
+    lands in a stack slot is passed as 32 bits)."""
+    from nvfp4bench_b200 import api
+    L = api.lib()
+    for name in api.EXPORTED:
+        fn = getattr(L, name)
+        if name in ("nvfp4_b200_version",):
+            continue
+        assert fn.argtypes is not None, name

@@ -121,7 +121,8 @@ def test_sm_pair_matches_one_sm(api):
 @pytest.mark.parametrize("shape", [(16, 14336, 4096), (64, 4096, 14336), (128, 1024, 2048),
                                    (1, 300, 512), (17, 1000, 96), (100, 2000, 4096),
                                    (33, 256, 8192), (32, 4096, 14336), (8, 2048, 4096),
-                                   (16, 4096, 14336)])
+                                   (16, 4096, 14336), (128, 4096, 14336), (128, 14336, 4096),
+                                   (5, 128, 1088), (64, 640, 320)])
 @pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
 def test_decode_kernel(api, orc, shape, out):
     """M <= 128 (the weight-streaming split-K kernel where the heuristic picks it, else the
@@ -131,8 +132,8 @@ def test_decode_kernel(api, orc, shape, out):
 
 
 def test_decode_repeat_deterministic(api):
-    """Split-K partial sums are reduced in split order by the last CTA: repeated calls agree
-    bit for bit (and the per-tile counters reset themselves)."""
+    """Split-K partial sums are reduced in cluster-rank order through distributed shared
+    memory: repeated calls agree bit for bit, and the BF16 output is the rounded FP32 one."""
     M, N, K = 16, 4096, 14336
     _, a = make_operand(api, M, K, 41)
     _, b = make_operand(api, N, K, 42)
