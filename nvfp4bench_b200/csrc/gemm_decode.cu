@@ -41,8 +41,7 @@ namespace {
 
 constexpr int kDThreads = 320;
 constexpr int kDTmemCols = 512;   // accumulator [0, 128) + kDSfSlots slots of 32 columns
-constexpr int kDSlotCols = 32;    // weight scales at +0 (4 per K-block), token scales at +16
-constexpr int kDSfSlots = 12;     // deep enough that the writer/MMA slot ring never throttles
+constexpr int kDSfSlots = 12;     // at most; deep enough that the slot ring never throttles
 constexpr int kDMaxCluster = 8;
 constexpr int kDSmemBudget = 200 * 1024;
 
@@ -57,20 +56,33 @@ struct DParams {
   uint32_t* err_word;
 };
 
+// A stage is KB K-blocks of 64: 8 (K = 512, two 128-byte-wide TMA boxes per operand) while
+// that leaves at least three stages, else 4. Per-stage costs (barrier waits, two commits,
+// fences: about 370 cycles measured beside the MMAs' own 4 x 46 cycles at N = 16) then fall
+// on twice the weight bytes; a 16 KB stage every ~620 cycles is what one SM's share of HBM
+// bandwidth delivers.
 template <int MPAD>
 struct DCfg {
-  static constexpr int kWBytes = 128 * 128;           // 128 weight rows x 256 FP4
-  static constexpr int kTBytes = MPAD * 128;          // MPAD token rows x 256 FP4
-  static constexpr int kSfBytes = 4 * 512;            // one 128-row atom per K-block
+  static constexpr int kKb = MPAD <= 64 ? 8 : 4;
+  static constexpr int kHalves = kKb / 4;             // 128-byte-wide boxes per operand
+  static constexpr int kWBytes = kHalves * 128 * 128; // 128 weight rows x 256 FP4 per box
+  static constexpr int kTBytes = kHalves * MPAD * 128;
+  static constexpr int kSfBytes = kKb * 512;          // one 128-row atom per K-block
   static constexpr int kStageBytes = kWBytes + kTBytes + 2 * kSfBytes;
   static constexpr int kStages0 = kDSmemBudget / kStageBytes;
   static constexpr int kStages = kStages0 > 10 ? 10 : kStages0;
+  // TMEM scale slot: weight scales at +4*kb (column 4*kb + q used by quadrant q), token
+  // scales at +4*kKb + 4*kb.
+  static constexpr int kSlotCols = 8 * kKb;
+  static constexpr int kSlots0 = (kDTmemCols - 128) / kSlotCols;
+  static constexpr int kSlots1 = kSlots0 < kDSfSlots ? kSlots0 : kDSfSlots;
+  // A writer's slot wait (the MMA of stage i - slots finished) must also order its "full"
+  // arrival after that barrier's previous phase (stage i - stages): slots <= stages.
+  static constexpr int kSlots = kSlots1 < kStages ? kSlots1 : kStages;
   static constexpr int kPartBytes = MPAD * 128 * 4;   // FP32 partial sums, [token][row]
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
   static_assert(kPartBytes <= kStages * kStageBytes, "partials reuse the stage memory");
-  // A writer's slot wait (the MMA of stage i - slots finished) must also order its "full"
-  // arrival after that barrier's previous phase (stage i - stages): slots <= stages.
-  static constexpr int kSlots = kDSfSlots < kStages ? kDSfSlots : kStages;
+  static_assert(kStages >= 3, "pipeline depth");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -158,19 +170,24 @@ __global__ void __launch_bounds__(kDThreads, 1)
           ok = false;
           break;
         }
-        int nkb = p.ka - kt * 4;
-        if (nkb > 4) nkb = 4;
+        int nkb = p.ka - kt * C::kKb;
+        if (nkb > C::kKb) nkb = C::kKb;
         const uint32_t sfb = static_cast<uint32_t>(nkb) * 512u;
         const uint32_t db = smem_u32(&sfd[s]);
         mbar_arrive_expect_tx(db, 2 * sfb);
         bulk_load(smem_u32(sSFW + s * C::kSfBytes),
-                  p.sfw + (static_cast<size_t>(tn) * p.ka + kt * 4) * 512, sfb, db);
-        bulk_load(smem_u32(sSFT + s * C::kSfBytes), p.sft + static_cast<size_t>(kt) * 4 * 512,
-                  sfb, db);
+                  p.sfw + (static_cast<size_t>(tn) * p.ka + kt * C::kKb) * 512, sfb, db);
+        bulk_load(smem_u32(sSFT + s * C::kSfBytes),
+                  p.sft + static_cast<size_t>(kt) * C::kKb * 512, sfb, db);
         const uint32_t fb = smem_u32(&full[s]);
         mbar_arrive_expect_tx(fb, C::kWBytes + C::kTBytes);
-        tma_load_2d(smem_u32(sW + s * C::kWBytes), &tmap_w, kt * 128, tn * 128, fb);
-        tma_load_2d(smem_u32(sT + s * C::kTBytes), &tmap_t, kt * 128, 0, fb);
+        // Boxes past the end of K read as zeros (and still count their bytes).
+#pragma unroll
+        for (int h = 0; h < C::kHalves; ++h) {
+          const int x = kt * C::kKb * 32 + h * 128;
+          tma_load_2d(smem_u32(sW + s * C::kWBytes + h * 128 * 128), &tmap_w, x, tn * 128, fb);
+          tma_load_2d(smem_u32(sT + s * C::kTBytes + h * MPAD * 128), &tmap_t, x, 0, fb);
+        }
       }
       if (!ok) {
         // The most recent fill of every stage lands before the CTA exits ("full" also counts
@@ -201,14 +218,23 @@ __global__ void __launch_bounds__(kDThreads, 1)
           break;
         }
         tc_fence_after();
-        int nkb = p.ka - kt * 4;
-        if (nkb > 4) nkb = 4;
-        const uint64_t ad0 = make_sdesc(smem_u32(sW + s * C::kWBytes), 16, 1024, 2);
-        const uint64_t bd0 = make_sdesc(smem_u32(sT + s * C::kTBytes), 16, 1024, 2);
-        const uint32_t sf_t = tmem_base + 128 + slot * kDSlotCols;
-        for (int kb = 0; kb < nkb; ++kb)
-          tc_mma_mxf4nvf4(tmem_base, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
-                          sf_t + 16 + kb * 4, (i > 0 || kb > 0) ? 1u : 0u);
+        int nkb = p.ka - kt * C::kKb;
+        if (nkb > C::kKb) nkb = C::kKb;
+        const uint32_t sf_t = tmem_base + 128 + slot * C::kSlotCols;
+        // K-block kb: box kb / 4, 32-byte step kb % 4 (+2 in 16-byte descriptor units).
+        auto mma = [&](int kb) {
+          const int h = kb >> 2, kk = kb & 3;
+          const uint64_t ad = make_sdesc(smem_u32(sW + s * C::kWBytes + h * 128 * 128), 16, 1024, 2);
+          const uint64_t bd = make_sdesc(smem_u32(sT + s * C::kTBytes + h * MPAD * 128), 16, 1024, 2);
+          tc_mma_mxf4nvf4(tmem_base, ad + 2 * kk, bd + 2 * kk, idesc, sf_t + kb * 4,
+                          sf_t + 4 * C::kKb + kb * 4, (i > 0 || kb > 0) ? 1u : 0u);
+        };
+        if (nkb == C::kKb) {
+#pragma unroll
+          for (int kb = 0; kb < C::kKb; ++kb) mma(kb);
+        } else {
+          for (int kb = 0; kb < nkb; ++kb) mma(kb);
+        }
         issued = true;
         tc_commit(smem_u32(&sf_empty[slot]));
         tc_commit(smem_u32(&empty[s]));
@@ -234,9 +260,9 @@ __global__ void __launch_bounds__(kDThreads, 1)
       // Weight rows are TMEM lanes: quadrant q's MMA rows read only word q of each atom row.
       // Token rows map to accumulator columns, read by every quadrant: all four words. Atoms
       // past the end of K hold stale bytes that no MMA reads.
-      uint32_t vw[4], vt[16];
+      uint32_t vw[C::kKb], vt[4 * C::kKb];
 #pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
+      for (int kb = 0; kb < C::kKb; ++kb) {
         vw[kb] = *reinterpret_cast<const uint32_t*>(sSFW + s * C::kSfBytes + kb * 512 + lane * 16 + q * 4);
         const uint4 t = *reinterpret_cast<const uint4*>(sSFT + s * C::kSfBytes + kb * 512 + lane * 16);
         vt[4 * kb] = t.x; vt[4 * kb + 1] = t.y; vt[4 * kb + 2] = t.z; vt[4 * kb + 3] = t.w;
@@ -246,10 +272,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
                      kErrWaitSfEmpty))
         break;
       tc_fence_after();
-      const uint32_t sf_t = lane_base + 128 + slot * kDSlotCols;
+      const uint32_t sf_t = lane_base + 128 + slot * C::kSlotCols;
 #pragma unroll
-      for (int kb = 0; kb < 4; ++kb) tmem_st_32x32b_x1(sf_t + kb * 4 + q, vw[kb]);
-      tmem_st_32x32b_x16(sf_t + 16, vt);
+      for (int kb = 0; kb < C::kKb; ++kb) tmem_st_32x32b_x1(sf_t + kb * 4 + q, vw[kb]);
+#pragma unroll
+      for (int c = 0; c < C::kKb / 4; ++c) tmem_st_32x32b_x16(sf_t + 4 * C::kKb + 16 * c, vt + 16 * c);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -337,6 +364,7 @@ template <int MPAD>
 bool launch_decode(const CUtensorMap& tw, const CUtensorMap& tt, DParams p, int sms,
                    DecodeState& st, int idx, cudaStream_t s, std::string* err) {
   using C = DCfg<MPAD>;
+  p.num_kt = (p.ka + C::kKb - 1) / C::kKb;
   if (!st.attr[idx]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_decode_kernel<MPAD>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
@@ -411,7 +439,7 @@ bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_
   p.alpha = op.a_global * op.b_global;
   p.out_bf16 = (op.d != nullptr && op.out_dtype == OutDType::BF16) ? 1 : 0;
   p.tiles_n = (op.N + 127) / 128;
-  p.num_kt = (op.K + 255) / 256;
+  p.num_kt = 0;  // K-stages: set per stage depth in launch_decode
   p.ka = (op.K + 63) / 64;
   p.splits = 1;
   p.err_word = device_error_word(err);
