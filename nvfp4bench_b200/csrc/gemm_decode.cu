@@ -43,7 +43,7 @@ constexpr int kDThreads = 320;
 constexpr int kDTmemCols = 512;   // accumulator [0, 128) + kDSfSlots slots of 32 columns
 constexpr int kDSfSlots = 12;     // at most; deep enough that the slot ring never throttles
 constexpr int kDMaxCluster = 8;
-constexpr int kDSmemBudget = 200 * 1024;
+constexpr int kDSmemBudget = 220 * 1024;
 
 struct DParams {
   const uint8_t* sfw;   // weight (MMA A side) scales, tcgen05 layout over N rows
@@ -56,14 +56,14 @@ struct DParams {
   uint32_t* err_word;
 };
 
-// A stage is KB K-blocks of 64: 8 (K = 512, two 128-byte-wide TMA boxes per operand) while
-// that leaves at least three stages, else 4. Per-stage costs (barrier waits, two commits,
+// A stage is KB = 8 K-blocks of 64 (K = 512, two 128-byte-wide TMA boxes per operand; at
+// least three stages fit for every token count). Per-stage costs (barrier waits, two commits,
 // fences: about 370 cycles measured beside the MMAs' own 4 x 46 cycles at N = 16) then fall
 // on twice the weight bytes; a 16 KB stage every ~620 cycles is what one SM's share of HBM
 // bandwidth delivers.
 template <int MPAD>
 struct DCfg {
-  static constexpr int kKb = MPAD <= 64 ? 8 : 4;
+  static constexpr int kKb = 8;                       // K-blocks per stage
   static constexpr int kHalves = kKb / 4;             // 128-byte-wide boxes per operand
   static constexpr int kWBytes = kHalves * 128 * 128; // 128 weight rows x 256 FP4 per box
   static constexpr int kTBytes = kHalves * MPAD * 128;
