@@ -38,6 +38,9 @@ CONFIGS = {
     # name: (M, N, K, out dtype, description)
     "c1": (1024, 1024, 1024, "f32", "NVFP4 GEMM 1024^3, FP32 out (BASELINE config 1)"),
     "c2": (4096, 14336, 4096, "bf16", "LLM FFN up-proj 4096x14336x4096, BF16 out (BASELINE config 2)"),
+    # BASELINE config 4 as the tcgen05 .sp kind::mxf4nvf4 MMA executes it on B200: 2 of the 4
+    # element pairs of every 8 K elements of A kept (seeded), UE4M3 scales per 32 K.
+    "c4": (4096, 14336, 8192, "bf16", "pair-wise 2:4 sparse NVFP4 4096x14336x8192, BF16 out (BASELINE config 4)"),
     "c3": (8192, 8192, 8192, "bf16", "square 8192^3, BF16 out (BASELINE config 3, 1 GPU)"),
     "decode-up-16": (16, 14336, 4096, "bf16", "decode M=16 up-proj"),
     "decode-up-64": (64, 14336, 4096, "bf16", "decode M=64 up-proj"),
@@ -47,10 +50,14 @@ CONFIGS = {
     "decode-down-128": (128, 4096, 14336, "bf16", "decode M=128 down-proj"),
 }
 SEED_A, SEED_B = 1234, 1234 ^ 0xABCDEF
+SEED_SPARSE = 0x24  # pair pattern of the sparse config
 
 
-def algorithmic_bytes(M, N, K, out_bytes):
-    """Operand values + scales read once, C written once (SURVEY roofline convention)."""
+def algorithmic_bytes(M, N, K, out_bytes, sparse=False):
+    """Operand values + scales read once, C written once (SURVEY roofline convention). Sparse:
+    A's kept values K/4 B + metadata K/16 B + scales K/32 B per row, B's scales K/32 B."""
+    if sparse:
+        return M * K / 4 + M * K / 16 + M * K / 32 + N * K / 2 + N * K / 32 + M * N * out_bytes
     return M * K / 2 + M * K / 16 + N * K / 2 + N * K / 16 + M * N * out_bytes
 
 
@@ -195,16 +202,27 @@ def run_b200(args, rank, world, local_rank):
     # weight seed offset by the rank.
     n0, n1 = shard_bounds(world * N, world, rank)
     assert n1 - n0 == N
+    sparse = args.config == "c4"
     x = api.fill_normal(M, K, SEED_A)
-    A = api.quantize(x, canonical=False, tcgen05=True)
+    a_meta = None
+    if sparse:
+        # Seeded pair pattern, pruned, quantised with 32-element scales, compressed.
+        a_meta = api.sparse_meta(M, K, SEED_SPARSE)
+        api.sparse_prune(x, a_meta)
+        A = api.quantize_block(x, 32, canonical=False, tcgen05=True)
+        A.packed = api.sparse_compress(A.packed, a_meta, K)
+    else:
+        A = api.quantize(x, canonical=False, tcgen05=True)
     del x
     x = api.fill_normal(N, K, SEED_B + rank)
-    B = api.quantize(x, canonical=False, tcgen05=True)
+    B = api.quantize_block(x, 32, canonical=False, tcgen05=True) if sparse else \
+        api.quantize(x, canonical=False, tcgen05=True)
     del x
     C = torch.empty((M, N), dtype=out_dtype, device=dev)
+    mode = api.MODE_SPARSE24 if sparse else api.MODE_DENSE
     gargs = api.gemm_args(A.packed, A.scales_tc, B.packed, B.scales_tc, M, N, K, C,
                           sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
-                          cta_group=args.cta_group)
+                          cta_group=args.cta_group, mode=mode, a_meta=a_meta)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
@@ -215,12 +233,16 @@ def run_b200(args, rank, world, local_rank):
     ladder = {}
     if not args.kernel_only:
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        for key, seed, sustained, reps in (("random_burst", 0x5EED, False, 5),
-                                           ("zero_burst", 0, False, 5),
-                                           ("random_sustained", 0x5EED, True, 2000)):
-            tf, mhz = api.peak_ex(256, 1, sms, 4096, reps, seed=seed, sustained=sustained)
+        # Burst rungs first: the sustained rung leaves the clock at its power-capped level.
+        rungs = [("random_burst", 0x5EED, False, 5, False), ("zero_burst", 0, False, 5, False)]
+        if sparse:
+            rungs.append(("sparse_random_burst", 0x5EED, False, 5, True))
+        rungs.append(("random_sustained", 0x5EED, True, 2000, False))
+        for key, seed, sustained, reps, sp in rungs:
+            tf, mhz = api.peak_ex(256, 1, sms, 4096, reps, seed=seed, sustained=sustained, sparse=sp)
             ladder[key] = {"tflops": round(tf, 1), "sm_mhz": round(mhz)}
-    peak_tf = ladder["random_burst"]["tflops"] if ladder else None
+    peak_key = "sparse_random_burst" if sparse else "random_burst"
+    peak_tf = ladder[peak_key]["tflops"] if ladder else None
 
     # Decode shapes (M <= 128) stream the weight once per step, and a flush that writes 256 MiB
     # leaves L2 full of dirty lines whose write-back competes with that stream. They use inputs
@@ -323,13 +345,15 @@ def run_b200(args, rank, world, local_rank):
     # e2e through the C ABI with pinned host buffers.
     hA, hAs = A.packed.cpu().pin_memory(), A.scales_tc.cpu().pin_memory()
     hB, hBs = B.packed.cpu().pin_memory(), B.scales_tc.cpu().pin_memory()
+    hM = a_meta.cpu().pin_memory() if sparse else None
     hC = torch.empty((M, N), dtype=out_dtype).pin_memory()
     dA, dAs = torch.empty_like(A.packed), torch.empty_like(A.scales_tc)
     dB, dBs = torch.empty_like(B.packed), torch.empty_like(B.scales_tc)
+    dM = torch.empty_like(a_meta) if sparse else None
     dC = torch.empty_like(C)
     eargs = api.gemm_args(dA, dAs, dB, dBs, M, N, K, dC, sf_layout=api.SF_TCGEN05,
-                          tile_n=args.tile_n, cta_group=args.cta_group)
-    h2d = hA.numel() + hAs.numel() + hB.numel() + hBs.numel()
+                          tile_n=args.tile_n, cta_group=args.cta_group, mode=mode, a_meta=dM)
+    h2d = hA.numel() + hAs.numel() + hB.numel() + hBs.numel() + (hM.numel() if sparse else 0)
     d2h = M * N * out_bytes
 
     def e2e_step():
@@ -337,6 +361,8 @@ def run_b200(args, rank, world, local_rank):
         dAs.copy_(hAs, non_blocking=True)
         dB.copy_(hB, non_blocking=True)
         dBs.copy_(hBs, non_blocking=True)
+        if sparse:
+            dM.copy_(hM, non_blocking=True)
         api.launch(eargs)
         hC.copy_(dC, non_blocking=True)
 
@@ -369,7 +395,7 @@ def run_b200(args, rank, world, local_rank):
     if os.path.exists(tfile):
         with open(tfile) as f:
             traffic = json.load(f).get(args.config)
-    abytes = algorithmic_bytes(M, N, K, out_bytes)
+    abytes = algorithmic_bytes(M, N, K, out_bytes, sparse)
     if M <= 128:
         # Decode shapes are HBM-bound: algorithmic bytes per launch / launch time against
         # the driver-measured copy bandwidth.
@@ -385,8 +411,10 @@ def run_b200(args, rank, world, local_rank):
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tf,
                     "unit": "TFLOP/s", "frac": achieved / peak_tf,
                     "peak_source": "tcgen05 kind::mxf4nvf4 ladder measured in this run "
-                                   "(M128 N256 K64 on every SM, random E2M1 operands, best "
-                                   "of 5 single launches)",
+                                   + ("(.sp M128 N256, 128 logical K per MMA, " if sparse else
+                                      "(M128 N256 K64, ")
+                                   + "on every SM, random E2M1 operands, best of 5 single "
+                                     "launches)",
                     "tcgen05_fp4_ladder": ladder,
                     "bf16_measured_peak": peaks.get("bf16_tflops"),
                     "traffic": traffic, "algorithmic_bytes": abytes}

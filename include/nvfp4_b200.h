@@ -83,6 +83,32 @@ int nvfp4_b200_dequantize(const void* packed, const void* scales, int rows, int 
                           float global_scale, float* out, void* stream, char* err,
                           size_t errlen);
 
+/* quantize / dequantize with `block` (16 or 32) elements per scale. Block 16 is the
+ * reference's NVFP4 codec (src/nvfp4.cu:62-112); block 32 is the same algorithm with the scale
+ * block the sparse tensor-core MMA applies (one UE4M3 scale per 32 K elements of A and of B).
+ * For block 32, scales are [rows][cols/32] and the tcgen05 layout takes
+ * nvfp4_b200_sf_tcgen05_bytes(rows, cols / 2) bytes. */
+int nvfp4_b200_quantize_ex(const float* src, int rows, int cols, float global_scale, int block,
+                           void* packed, void* scales, void* scales_tcgen05, void* stream,
+                           char* err, size_t errlen);
+int nvfp4_b200_dequantize_ex(const void* packed, const void* scales, int rows, int cols,
+                             float global_scale, int block, float* out, void* stream, char* err,
+                             size_t errlen);
+
+/* Pair-wise 2:4 structured sparsity of A (GemmMode::Sparse; the reference has no data path,
+ * src/gemm_custom.cu:135-139). The tcgen05 .sp kind::mxf4nvf4 MMA keeps 2 of the 4 element
+ * pairs of every group of 8 consecutive K elements. meta [rows][K/16]: one nibble per group
+ * (first kept pair | second << 2; the even group in the low nibble), drawn per group i =
+ * row*K/8 + g as splitmix64(seed + (i+1)*golden) % 6 over {01,02,03,12,13,23}. prune zeroes the
+ * dropped pairs of an fp32 [rows][K] matrix in place; compress turns packed [rows][K/2] into
+ * the kept values [rows][K/4] (one byte per kept pair, in order). K % 16 == 0. */
+int nvfp4_b200_sparse_meta(int rows, int K, uint64_t seed, void* meta, void* stream, char* err,
+                           size_t errlen);
+int nvfp4_b200_sparse_prune(float* a, int rows, int K, const void* meta, void* stream, char* err,
+                            size_t errlen);
+int nvfp4_b200_sparse_compress(const void* packed, int rows, int K, const void* meta,
+                               void* values, void* stream, char* err, size_t errlen);
+
 /* Replaces make_random_matrix - src/nvfp4.h:47-48, src/nvfp4.cu:115-129 - on the GPU,
  * bit-identical (splitmix64 -> uniform [-1,1)). */
 int nvfp4_b200_fill_uniform(float* out, int rows, int cols, uint64_t seed, void* stream,
@@ -122,10 +148,12 @@ int nvfp4_b200_peak(int n, int ctas, int iters, int reps, double* tflops, void* 
  * SM pairs of M=256 x 256 MMAs. seed 0 stages zero operands, any other value pseudo-random
  * E2M1 bytes (the data sets the power drawn and so, under the power cap, the clock).
  * sustained 0: best of `reps` single timed launches; 1: mean over `reps` back-to-back
- * launches. *sm_mhz (may be NULL) gets the SM clock CTA 0 ran at (clock64 / globaltimer). */
+ * launches. sparse 1 (cta_group 1): tcgen05.mma.sp rungs (128 logical K per MMA, FLOPs counted
+ * on the logical K; the reference's sparse rungs, src/peak.cu:46-68,93-115). *sm_mhz (may be
+ * NULL) gets the SM clock CTA 0 ran at (clock64 / globaltimer). */
 int nvfp4_b200_peak_ex(int n, int cta_group, int units, int iters, int reps, uint32_t seed,
-                       int sustained, double* tflops, double* sm_mhz, void* stream, char* err,
-                       size_t errlen);
+                       int sustained, int sparse, double* tflops, double* sm_mhz, void* stream,
+                       char* err, size_t errlen);
 
 /* Reads (and when clear != 0 resets) the device error word the kernels write when a
  * bounded wait times out (bit meanings in nvfp4bench_b200/csrc/ptx.cuh). Synchronises

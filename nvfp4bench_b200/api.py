@@ -30,6 +30,8 @@ EXPORTED = [
     "nvfp4_b200_sf_to_tcgen05", "nvfp4_b200_measure_bandwidth", "nvfp4_b200_peak",
     "nvfp4_b200_device_error", "nvfp4_b200_wait_selftest", "nvfp4_b200_version",
     "nvfp4_b200_gemm_noalloc", "nvfp4_b200_gemm_noalloc_scratch_bytes", "nvfp4_b200_peak_ex",
+    "nvfp4_b200_quantize_ex", "nvfp4_b200_dequantize_ex", "nvfp4_b200_sparse_meta",
+    "nvfp4_b200_sparse_prune", "nvfp4_b200_sparse_compress",
 ]
 
 
@@ -72,6 +74,11 @@ def lib():
         L.nvfp4_b200_gemm_noalloc_scratch_bytes.restype = sz
         L.nvfp4_b200_quantize.argtypes = [vp, ip, ip, C.c_float, vp, vp, vp, vp, *errs]
         L.nvfp4_b200_dequantize.argtypes = [vp, vp, ip, ip, C.c_float, vp, vp, *errs]
+        L.nvfp4_b200_quantize_ex.argtypes = [vp, ip, ip, C.c_float, ip, vp, vp, vp, vp, *errs]
+        L.nvfp4_b200_dequantize_ex.argtypes = [vp, vp, ip, ip, C.c_float, ip, vp, vp, *errs]
+        L.nvfp4_b200_sparse_meta.argtypes = [ip, ip, C.c_uint64, vp, vp, *errs]
+        L.nvfp4_b200_sparse_prune.argtypes = [vp, ip, ip, vp, vp, *errs]
+        L.nvfp4_b200_sparse_compress.argtypes = [vp, ip, ip, vp, vp, vp, *errs]
         L.nvfp4_b200_fill_uniform.argtypes = [vp, ip, ip, C.c_uint64, vp, *errs]
         L.nvfp4_b200_fill_normal.argtypes = [vp, ip, ip, C.c_uint64, vp, *errs]
         L.nvfp4_b200_sf_tcgen05_bytes.argtypes = [ip, ip]
@@ -80,8 +87,8 @@ def lib():
         L.nvfp4_b200_measure_bandwidth.argtypes = [ip, vp, vp, vp, sz, ip,
                                                    C.POINTER(C.c_double), vp, *errs]
         L.nvfp4_b200_peak.argtypes = [ip, ip, ip, ip, C.POINTER(C.c_double), vp, *errs]
-        L.nvfp4_b200_peak_ex.argtypes = [ip, ip, ip, ip, ip, C.c_uint32, ip, C.POINTER(C.c_double),
-                                         C.POINTER(C.c_double), vp, *errs]
+        L.nvfp4_b200_peak_ex.argtypes = [ip, ip, ip, ip, ip, C.c_uint32, ip, ip,
+                                         C.POINTER(C.c_double), C.POINTER(C.c_double), vp, *errs]
         L.nvfp4_b200_device_error.argtypes = [ip, C.POINTER(C.c_uint32), *errs]
         L.nvfp4_b200_wait_selftest.argtypes = [C.c_uint64, C.POINTER(C.c_uint32), *errs]
         L.nvfp4_b200_version.restype = C.c_char_p
@@ -183,6 +190,52 @@ def dequantize(t: Nvfp4Tensor, stream=None) -> torch.Tensor:
     return out
 
 
+def quantize_block(x: torch.Tensor, block: int, global_scale: float = 1.0, canonical: bool = True,
+                   tcgen05: bool = True, stream=None) -> Nvfp4Tensor:
+    """quantize() with `block` (16 or 32) elements per scale; block 32 is the scale block of the
+    sparse MMA (scales [rows, cols/32]; tcgen05 layout of a [rows, cols/2] block-16 operand)."""
+    assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous() and x.dim() == 2
+    rows, cols = x.shape
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=x.device)
+    sc = torch.empty((rows, cols // block), dtype=torch.uint8, device=x.device) if canonical else None
+    vcols = cols if block == 16 else cols // 2
+    tc = torch.empty(sf_tcgen05_bytes(rows, vcols), dtype=torch.uint8, device=x.device) \
+        if tcgen05 else None
+    _call(lib().nvfp4_b200_quantize_ex, x.data_ptr(), rows, cols, global_scale, block,
+          packed.data_ptr(), _ptr(sc), _ptr(tc), _stream(stream))
+    return Nvfp4Tensor(rows, cols, global_scale, packed, sc, tc)
+
+
+def dequantize_block(t: Nvfp4Tensor, block: int, stream=None) -> torch.Tensor:
+    out = torch.empty((t.rows, t.cols), dtype=torch.float32, device=t.packed.device)
+    _call(lib().nvfp4_b200_dequantize_ex, t.packed.data_ptr(), t.scales.data_ptr(), t.rows, t.cols,
+          t.global_scale, block, out.data_ptr(), _stream(stream))
+    return out
+
+
+def sparse_meta(rows: int, K: int, seed: int, device="cuda", stream=None) -> torch.Tensor:
+    """Pair-wise 2:4 metadata uint8 [rows, K/16] (see nvfp4_b200_sparse_meta)."""
+    out = torch.empty((rows, K // 16), dtype=torch.uint8, device=device)
+    _call(lib().nvfp4_b200_sparse_meta, rows, K, C.c_uint64(seed), out.data_ptr(), _stream(stream))
+    return out
+
+
+def sparse_prune(a: torch.Tensor, meta: torch.Tensor, stream=None) -> torch.Tensor:
+    """Zero the dropped pairs of fp32 [rows, K] in place; returns `a`."""
+    rows, K = a.shape
+    _call(lib().nvfp4_b200_sparse_prune, a.data_ptr(), rows, K, meta.data_ptr(), _stream(stream))
+    return a
+
+
+def sparse_compress(packed: torch.Tensor, meta: torch.Tensor, K: int, stream=None) -> torch.Tensor:
+    """packed [rows, K/2] -> kept values [rows, K/4]."""
+    rows = packed.shape[0]
+    out = torch.empty((rows, K // 4), dtype=torch.uint8, device=packed.device)
+    _call(lib().nvfp4_b200_sparse_compress, packed.data_ptr(), rows, K, meta.data_ptr(),
+          out.data_ptr(), _stream(stream))
+    return out
+
+
 def fill_uniform(rows: int, cols: int, seed: int, device="cuda", stream=None) -> torch.Tensor:
     out = torch.empty((rows, cols), dtype=torch.float32, device=device)
     _call(lib().nvfp4_b200_fill_uniform, out.data_ptr(), rows, cols, seed, _stream(stream))
@@ -218,12 +271,12 @@ def peak(n: int = 256, ctas: int = 148, iters: int = 4096, reps: int = 5, stream
 
 
 def peak_ex(n: int = 256, cta_group: int = 1, units: int = 148, iters: int = 4096, reps: int = 5,
-            seed: int = 0, sustained: bool = False, stream=None) -> tuple:
+            seed: int = 0, sustained: bool = False, sparse: bool = False, stream=None) -> tuple:
     """(TFLOP/s, SM MHz of CTA 0) of one ladder rung; see nvfp4_b200_peak_ex."""
     t = C.c_double(0.0)
     mhz = C.c_double(0.0)
     _call(lib().nvfp4_b200_peak_ex, n, cta_group, units, iters, reps, C.c_uint32(seed),
-          1 if sustained else 0, C.byref(t), C.byref(mhz), _stream(stream))
+          1 if sustained else 0, 1 if sparse else 0, C.byref(t), C.byref(mhz), _stream(stream))
     return t.value, mhz.value
 
 

@@ -138,6 +138,56 @@ int nvfp4_b200_dequantize(const void* packed, const void* scales, int rows, int 
   return ok(err, errlen);
 }
 
+int nvfp4_b200_quantize_ex(const float* src, int rows, int cols, float global_scale, int block,
+                           void* packed, void* scales, void* scales_tc, void* stream, char* err,
+                           size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::quantize_block(src, rows, cols, global_scale, block, static_cast<uint8_t*>(packed),
+                                 static_cast<uint8_t*>(scales), static_cast<uint8_t*>(scales_tc),
+                                 static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_dequantize_ex(const void* packed, const void* scales, int rows, int cols,
+                             float global_scale, int block, float* out, void* stream, char* err,
+                             size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::dequantize_block(static_cast<const uint8_t*>(packed),
+                                   static_cast<const uint8_t*>(scales), rows, cols, global_scale,
+                                   block, out, static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_sparse_meta(int rows, int K, uint64_t seed, void* meta, void* stream, char* err,
+                           size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::sparse_meta(rows, K, seed, static_cast<uint8_t*>(meta),
+                              static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_sparse_prune(float* a, int rows, int K, const void* meta, void* stream, char* err,
+                            size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::sparse_prune(a, rows, K, static_cast<const uint8_t*>(meta),
+                               static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
+int nvfp4_b200_sparse_compress(const void* packed, int rows, int K, const void* meta, void* values,
+                               void* stream, char* err, size_t errlen) {
+  std::string e;
+  if (!nvfp4b200::sparse_compress(static_cast<const uint8_t*>(packed), rows, K,
+                                  static_cast<const uint8_t*>(meta), static_cast<uint8_t*>(values),
+                                  static_cast<cudaStream_t>(stream), &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
 int nvfp4_b200_fill_uniform(float* out, int rows, int cols, uint64_t seed, void* stream, char* err,
                             size_t errlen) {
   if (rows < 0 || cols < 0) return fail(NVFP4_B200_EINVAL, "negative size", err, errlen);
@@ -191,10 +241,10 @@ int nvfp4_b200_peak(int n, int ctas, int iters, int reps, double* tflops, void* 
 }
 
 int nvfp4_b200_peak_ex(int n, int cta_group, int units, int iters, int reps, uint32_t seed,
-                       int sustained, double* tflops, double* sm_mhz, void* stream, char* err,
-                       size_t errlen) {
+                       int sustained, int sparse, double* tflops, double* sm_mhz, void* stream,
+                       char* err, size_t errlen) {
   std::string e;
-  const nvfp4b200::PeakOptions o{n, cta_group, units, iters, reps, seed, sustained};
+  const nvfp4b200::PeakOptions o{n, cta_group, units, iters, reps, seed, sustained, sparse};
   if (!nvfp4b200::peak_ladder_ex(o, tflops, sm_mhz, static_cast<cudaStream_t>(stream), &e))
     return fail(classify(e), e, err, errlen);
   return ok(err, errlen);

@@ -99,25 +99,27 @@ __global__ void fill_normal_kernel(float* __restrict__ out, size_t n, uint64_t x
   }
 }
 
-// One thread per 16-element block (src/nvfp4.cu:66-95).
+// One thread per BLK-element block (src/nvfp4.cu:66-95 with BLK = 16; BLK = 32 is the scale
+// block of the sparse tensor-core MMA). ka = tcgen05 atoms per 128-row block along K.
+template <int BLK>
 __global__ void quantize_kernel(const float* __restrict__ src, int rows, int cols, float g,
                                 uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
                                 uint8_t* __restrict__ scales_tc, int ka) {
-  const int nb = cols / 16;
+  const int nb = cols / BLK;
   const size_t nblocks = static_cast<size_t>(rows) * nb;
   for (size_t blk = blockIdx.x * size_t(blockDim.x) + threadIdx.x; blk < nblocks;
        blk += size_t(gridDim.x) * blockDim.x) {
     const int r = static_cast<int>(blk / nb), b = static_cast<int>(blk % nb);
-    const float4* x4 = reinterpret_cast<const float4*>(src + static_cast<size_t>(r) * cols + b * 16);
-    float x[16];
+    const float4* x4 = reinterpret_cast<const float4*>(src + static_cast<size_t>(r) * cols + b * BLK);
+    float x[BLK];
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
+    for (int v = 0; v < BLK / 4; ++v) {
       const float4 t = x4[v];
       x[4 * v] = t.x; x[4 * v + 1] = t.y; x[4 * v + 2] = t.z; x[4 * v + 3] = t.w;
     }
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < BLK; ++j) {
       const float a = fabsf(x[j]);
       if (amax < a) amax = a;  // std::max(amax, a): NaN never replaces amax
     }
@@ -125,12 +127,17 @@ __global__ void quantize_kernel(const float* __restrict__ src, int rows, int col
     const uint8_t sc = e4m3_encode_dev(scale);
     float dec = __fmul_rn(e4m3_decode_dev(sc), g);
     if (dec <= 0.0f) dec = 1.0f;
-    uint32_t lo = 0, hi = 0;
+    uint32_t w[BLK / 8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) lo |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[j], dec))) << (4 * j);
+    for (int q = 0; q < BLK / 8; ++q) {
+      w[q] = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) hi |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[8 + j], dec))) << (4 * j);
-    *reinterpret_cast<uint2*>(packed + (static_cast<size_t>(r) * cols + b * 16) / 2) = make_uint2(lo, hi);
+      for (int j = 0; j < 8; ++j)
+        w[q] |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[8 * q + j], dec))) << (4 * j);
+    }
+    uint8_t* dst = packed + (static_cast<size_t>(r) * cols + b * BLK) / 2;
+    if (BLK == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[BLK / 8 > 2 ? 2 : 0], w[BLK / 8 > 3 ? 3 : 0]);
     if (scales) scales[blk] = sc;
     if (scales_tc) {
       const size_t atom = static_cast<size_t>(r / 128) * ka + b / 4;
@@ -139,15 +146,17 @@ __global__ void quantize_kernel(const float* __restrict__ src, int rows, int col
   }
 }
 
-// src/nvfp4.cu:99-112, one thread per 16-element block.
+// src/nvfp4.cu:99-112, one thread per 16-element half-block of a BLK-element scale block.
+template <int BLK>
 __global__ void dequantize_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ scales,
                                   int rows, int cols, float g, float* __restrict__ out) {
-  const int nb = cols / 16;
-  const size_t nblocks = static_cast<size_t>(rows) * nb;
-  for (size_t blk = blockIdx.x * size_t(blockDim.x) + threadIdx.x; blk < nblocks;
-       blk += size_t(gridDim.x) * blockDim.x) {
-    const float s = __fmul_rn(e4m3_decode_dev(scales[blk]), g);
-    const size_t e0 = (blk / nb) * static_cast<size_t>(cols) + (blk % nb) * 16;
+  const int nh = cols / 16;
+  const size_t nhalves = static_cast<size_t>(rows) * nh;
+  for (size_t h = blockIdx.x * size_t(blockDim.x) + threadIdx.x; h < nhalves;
+       h += size_t(gridDim.x) * blockDim.x) {
+    const size_t r = h / nh, c0 = (h % nh) * 16;
+    const float s = __fmul_rn(e4m3_decode_dev(scales[r * (cols / BLK) + c0 / BLK]), g);
+    const size_t e0 = r * static_cast<size_t>(cols) + c0;
     const uint2 w = *reinterpret_cast<const uint2*>(packed + e0 / 2);
     float4* o = reinterpret_cast<float4*>(out + e0);
 #pragma unroll
@@ -162,7 +171,59 @@ __global__ void dequantize_kernel(const uint8_t* __restrict__ packed, const uint
   }
 }
 
-// Canonical [rows][K/16] -> tcgen05 atoms; one thread per output 32-bit word, zero padding.
+// ---- pair-wise 2:4 sparsity (the pattern of the tcgen05 .sp kind::mxf4nvf4 MMA) ----------
+// Each group of 8 consecutive K elements of an A row is 4 element pairs, 2 of them kept.
+// Group i (row-major over rows x K/8) keeps combination splitmix64(seed + (i+1)*golden) % 6 of
+// {01, 02, 03, 12, 13, 23}; its metadata nibble is first | second << 2, two groups per byte.
+__constant__ uint8_t kSpLo[6] = {0, 0, 0, 1, 1, 2};
+__constant__ uint8_t kSpHi[6] = {1, 2, 3, 2, 3, 3};
+
+__global__ void sparse_meta_kernel(uint8_t* __restrict__ meta, size_t nbytes, uint64_t seed) {
+  for (size_t j = blockIdx.x * size_t(blockDim.x) + threadIdx.x; j < nbytes;
+       j += size_t(gridDim.x) * blockDim.x) {
+    uint32_t b = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint64_t i = 2 * j + h;
+      const unsigned p = static_cast<unsigned>(splitmix_mix(seed + (i + 1) * kGolden) % 6);
+      b |= static_cast<uint32_t>(kSpLo[p] | (kSpHi[p] << 2)) << (4 * h);
+    }
+    meta[j] = static_cast<uint8_t>(b);
+  }
+}
+
+// Zero the two dropped pairs of every group of an fp32 [rows][K] matrix, in place.
+__global__ void sparse_prune_kernel(float* __restrict__ a, const uint8_t* __restrict__ meta, size_t ngroups) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < ngroups;
+       i += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t nib = (meta[i / 2] >> (4 * (i & 1))) & 0xF;
+    float4* g4 = reinterpret_cast<float4*>(a + i * 8);
+    float4 lo = g4[0], hi = g4[1];
+    const uint32_t keep = (1u << (nib & 3)) | (1u << ((nib >> 2) & 3));
+    if (!(keep & 1u)) { lo.x = 0.0f; lo.y = 0.0f; }
+    if (!(keep & 2u)) { lo.z = 0.0f; lo.w = 0.0f; }
+    if (!(keep & 4u)) { hi.x = 0.0f; hi.y = 0.0f; }
+    if (!(keep & 8u)) { hi.z = 0.0f; hi.w = 0.0f; }
+    g4[0] = lo;
+    g4[1] = hi;
+  }
+}
+
+// packed [rows][K/2] -> values [rows][K/4]: one pair is one byte; a metadata byte (2 groups)
+// turns 8 packed bytes into 4 value bytes.
+__global__ void sparse_compress_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ meta,
+                                       uint8_t* __restrict__ values, size_t nbytes) {
+  for (size_t j = blockIdx.x * size_t(blockDim.x) + threadIdx.x; j < nbytes;
+       j += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t m = meta[j];
+    const uint2 w = *reinterpret_cast<const uint2*>(packed + 8 * j);
+    auto byte_of = [](uint32_t word, uint32_t k) { return (word >> (8 * k)) & 0xFFu; };
+    const uint32_t v = byte_of(w.x, m & 3) | (byte_of(w.x, (m >> 2) & 3) << 8) |
+                       (byte_of(w.y, (m >> 4) & 3) << 16) | (byte_of(w.y, (m >> 6) & 3) << 24);
+    *reinterpret_cast<uint32_t*>(values + 4 * j) = v;
+  }
+}
+
 __global__ void sf_to_tcgen05_kernel(const uint8_t* __restrict__ scales, int rows, int ns, int ka,
                                      size_t words, uint32_t* __restrict__ out) {
   for (size_t w = blockIdx.x * size_t(blockDim.x) + threadIdx.x; w < words;
@@ -218,46 +279,108 @@ bool fill_normal(float* out, size_t n, uint64_t seed, cudaStream_t s, std::strin
   return check_launch("fill_normal", err);
 }
 
-bool quantize(const float* src, int rows, int cols, float global_scale, uint8_t* packed,
-              uint8_t* scales, uint8_t* scales_tc, cudaStream_t s, std::string* err) {
+bool quantize_block(const float* src, int rows, int cols, float global_scale, int block,
+                    uint8_t* packed, uint8_t* scales, uint8_t* scales_tc, cudaStream_t s,
+                    std::string* err) {
   if (!src || !packed) { set_err(err, "null pointer"); return false; }
-  if (rows < 0 || cols < 0 || cols % 16 != 0) {
-    set_err(err, "quantize needs rows >= 0 and cols a multiple of 16");
+  if (block != 16 && block != 32) { set_err(err, "quantize block must be 16 or 32"); return false; }
+  if (rows < 0 || cols < 0 || cols % block != 0) {
+    set_err(err, "quantize needs rows >= 0 and cols a multiple of the block (16 or 32)");
     return false;
   }
-  if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(packed) & 7)) {
-    set_err(err, "quantize needs a 16-byte aligned source and an 8-byte aligned packed output");
+  if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(packed) & (block == 16 ? 7 : 15))) {
+    set_err(err, "quantize needs a 16-byte aligned source and an 8-byte (16-byte for block 32) aligned packed output");
     return false;
   }
-  const size_t nblocks = static_cast<size_t>(rows) * (cols / 16);
+  const size_t nblocks = static_cast<size_t>(rows) * (cols / block);
   if (nblocks == 0) return true;
+  // Block 32: atoms of 128 rows x 4 scales cover 128 K, the same atom layout over cols / 2.
+  const int vcols = block == 16 ? cols : cols / 2;
   if (scales_tc) {
-    if (cudaMemsetAsync(scales_tc, 0, sf_tcgen05_bytes(rows, cols), s) != cudaSuccess) {
+    if (cudaMemsetAsync(scales_tc, 0, sf_tcgen05_bytes(rows, vcols), s) != cudaSuccess) {
       set_err(err, "cudaMemsetAsync of the tcgen05 scale buffer failed");
       return false;
     }
   }
-  quantize_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(src, rows, cols, global_scale, packed,
-                                                        scales, scales_tc, (cols + 63) / 64);
+  const int ka = (vcols + 63) / 64;
+  if (block == 16)
+    quantize_kernel<16><<<grid_for(nblocks, 256), 256, 0, s>>>(src, rows, cols, global_scale, packed,
+                                                              scales, scales_tc, ka);
+  else
+    quantize_kernel<32><<<grid_for(nblocks, 256), 256, 0, s>>>(src, rows, cols, global_scale, packed,
+                                                              scales, scales_tc, ka);
   return check_launch("quantize", err);
 }
 
-bool dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
-                float global_scale, float* out, cudaStream_t s, std::string* err) {
+bool quantize(const float* src, int rows, int cols, float global_scale, uint8_t* packed,
+              uint8_t* scales, uint8_t* scales_tc, cudaStream_t s, std::string* err) {
+  return quantize_block(src, rows, cols, global_scale, 16, packed, scales, scales_tc, s, err);
+}
+
+bool dequantize_block(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                      float global_scale, int block, float* out, cudaStream_t s, std::string* err) {
   if (!packed || !scales || !out) { set_err(err, "null pointer"); return false; }
-  if (rows < 0 || cols < 0 || cols % 16 != 0) {
-    set_err(err, "dequantize needs cols a multiple of 16");
+  if (block != 16 && block != 32) { set_err(err, "dequantize block must be 16 or 32"); return false; }
+  if (rows < 0 || cols < 0 || cols % block != 0) {
+    set_err(err, "dequantize needs cols a multiple of the block (16 or 32)");
     return false;
   }
   if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(packed) & 7)) {
     set_err(err, "dequantize needs a 16-byte aligned output and an 8-byte aligned packed input");
     return false;
   }
-  const size_t nblocks = static_cast<size_t>(rows) * (cols / 16);
-  if (nblocks == 0) return true;
-  dequantize_kernel<<<grid_for(nblocks, 256), 256, 0, s>>>(packed, scales, rows, cols,
-                                                          global_scale, out);
+  const size_t nhalves = static_cast<size_t>(rows) * (cols / 16);
+  if (nhalves == 0) return true;
+  if (block == 16)
+    dequantize_kernel<16><<<grid_for(nhalves, 256), 256, 0, s>>>(packed, scales, rows, cols,
+                                                                global_scale, out);
+  else
+    dequantize_kernel<32><<<grid_for(nhalves, 256), 256, 0, s>>>(packed, scales, rows, cols,
+                                                                global_scale, out);
   return check_launch("dequantize", err);
+}
+
+bool dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                float global_scale, float* out, cudaStream_t s, std::string* err) {
+  return dequantize_block(packed, scales, rows, cols, global_scale, 16, out, s, err);
+}
+
+bool sparse_meta(int rows, int K, uint64_t seed, uint8_t* meta, cudaStream_t s, std::string* err) {
+  if (!meta) { set_err(err, "null pointer"); return false; }
+  if (rows < 0 || K < 0 || K % 16 != 0) {
+    set_err(err, "sparse metadata needs K a multiple of 16");
+    return false;
+  }
+  const size_t nbytes = static_cast<size_t>(rows) * (K / 16);
+  if (nbytes == 0) return true;
+  sparse_meta_kernel<<<grid_for(nbytes, 256), 256, 0, s>>>(meta, nbytes, seed);
+  return check_launch("sparse_meta", err);
+}
+
+bool sparse_prune(float* a, int rows, int K, const uint8_t* meta, cudaStream_t s, std::string* err) {
+  if (!a || !meta) { set_err(err, "null pointer"); return false; }
+  if (rows < 0 || K < 0 || K % 16 != 0 || (reinterpret_cast<uintptr_t>(a) & 15)) {
+    set_err(err, "sparse prune needs K a multiple of 16 and a 16-byte aligned matrix");
+    return false;
+  }
+  const size_t ngroups = static_cast<size_t>(rows) * (K / 8);
+  if (ngroups == 0) return true;
+  sparse_prune_kernel<<<grid_for(ngroups, 256), 256, 0, s>>>(a, meta, ngroups);
+  return check_launch("sparse_prune", err);
+}
+
+bool sparse_compress(const uint8_t* packed, int rows, int K, const uint8_t* meta, uint8_t* values,
+                     cudaStream_t s, std::string* err) {
+  if (!packed || !meta || !values) { set_err(err, "null pointer"); return false; }
+  if (rows < 0 || K < 0 || K % 16 != 0 || (reinterpret_cast<uintptr_t>(packed) & 7) ||
+      (reinterpret_cast<uintptr_t>(values) & 3)) {
+    set_err(err, "sparse compress needs K a multiple of 16, packed 8-byte and values 4-byte aligned");
+    return false;
+  }
+  const size_t nbytes = static_cast<size_t>(rows) * (K / 16);
+  if (nbytes == 0) return true;
+  sparse_compress_kernel<<<grid_for(nbytes, 256), 256, 0, s>>>(packed, meta, values, nbytes);
+  return check_launch("sparse_compress", err);
 }
 
 bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStream_t s,

@@ -115,7 +115,8 @@ struct GemmParams {
   int tma_store;        // 1: epilogue stores through the C tensor map
   int tiles_m, tiles_n, num_tiles;
   int group_m;
-  int ka;               // scale atoms along K = ceil(K/64)
+  int ka;               // scale atoms along K = ceil(K/64) (sparse: ceil(K/128))
+  const uint8_t* meta;  // sparse: pair metadata [M][K/16]
   int num_kt;           // K-stages = ceil(K/256)
   int sfb_rowblocks;    // ceil(N/128)
   int sfa_rowblocks;    // ceil(M/128)
@@ -551,6 +552,275 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 }
 
 
+// ---- pair-wise 2:4 sparse kernel (tcgen05.mma.sp): 128 x 128 tiles ---------------------
+// A is stored compressed ([M][K/4] bytes: the 2 kept pairs of every group of 8 K elements)
+// with pair metadata [M][K/16] (a nibble per group: first kept pair | second << 2) and
+// UE4M3 scales per 32 K elements (A and B); B is dense. One sparse MMA covers 128 logical K
+// (32 compressed bytes of A, 64 bytes of B); a stage is 512 logical K, four MMAs: A 16 KB
+// (one 128-byte-wide box) + B 32 KB (two boxes), four stages. The MMA reads, per row and per
+// MMA, one word of A scales and one of B scales (byte j for logical K 32j..32j+31), and two
+// TMEM columns of metadata in the row's own lane (measured on B200 with one-hot probes). The
+// writers load all three from L2 into registers and store them into a ring of two TMEM slots:
+// SFA one column per quadrant (diagonal, as in the dense kernel), SFB whole in every quadrant,
+// metadata 8 columns in the rows' own lanes. Accumulators: two 128-column buffers, no overlap.
+struct SpCfg {
+  static constexpr int kABytes = 128 * 128;                 // 128 rows x 128 B compressed
+  static constexpr int kBBox = 128 * 128;                   // 128 rows x 128 B of B
+  static constexpr int kBBytes = 2 * kBBox;                 // 128 rows x 256 B (512 K)
+  static constexpr int kStageBytes = kABytes + kBBytes;     // 48 KB
+  static constexpr int kStages = 4;
+  static constexpr int kMmas = 4;                           // per stage
+  static constexpr int kCBufBytes = 32 * 32 * 4;
+  static constexpr int kCBytes = 4 * 2 * kCBufBytes;
+  static constexpr int kBarBytes = 512;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
+  static constexpr int kSfSlots = 2;
+  static constexpr int kSlotCols = 48;                      // SFA +0, SFB +16, metadata +32
+  static constexpr int kSfCol = 256;                        // after the two accumulators
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kSfCol + kSfSlots * kSlotCols <= kTmemCols, "TMEM budget");
+};
+
+__device__ __forceinline__ void tc_mma_mxf4nvf4_sp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                   uint32_t meta_tmem, uint32_t idesc, uint32_t sfa_tmem,
+                                                   uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %7, 0;\n\t"
+      "tcgen05.mma.sp.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X "
+      "[%0], %1, %2, [%3], %4, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem),
+      "r"(accumulate)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_sparse_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                       const __grid_constant__ CUtensorMap tmap_b,
+                       const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
+  using C = SpCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + C::kStages * C::kABytes;
+  uint8_t* sC = sB + C::kStages * C::kBBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
+  uint64_t* full = bars;                      // A/B bytes + producer + the stage's 4 writers
+  uint64_t* empty = full + C::kStages;
+  uint64_t* sf_empty = empty + C::kStages;
+  uint64_t* acc_full = sf_empty + C::kSfSlots;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1 + 4);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int j = 0; j < C::kSfSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 4);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    if (p.tma_store) prefetch_tmap(&tmap_c);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(p, t, tm, tn);
+        for (int kt = 0; kt < p.num_kt; ++kt, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+          if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word,
+                         kErrWaitSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes);
+          // Boxes past the end of K read as zeros (and still count their bytes).
+          tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * 128, tm * 128, fb);
+          tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * 256, tn * 128, fb);
+          tma_load_2d(smem_u32(sB + s * C::kBBytes + C::kBBox), &tmap_b, kt * 256 + 128, tn * 128, fb);
+        }
+      }
+      if (!ok) {
+        for (int back = 1; back <= C::kStages && it - back >= 0; ++back) {
+          const int f = it - back;
+          mbar_wait_drain(smem_u32(&full[f % C::kStages]),
+                          static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_mxf4nvf4(kBM, 128) | (1u << 2);  // bit 2: sparse A
+      int it = 0, local = 0;
+      bool ok = true, issued = false;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+        const int b = local & 1;
+        const uint32_t u = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(smem_u32(&acc_empty[b]), (u & 1u) ^ 1u, abort_flag, p.err_word,
+                       kErrWaitAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc_t = tmem_base + (b ? 128u : 0u);
+        for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
+          if (!mbar_spin_wait<false>(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word,
+                                     kErrWaitTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int slot = it % C::kSfSlots;
+          int nm = p.ka - kt * C::kMmas;
+          if (nm > C::kMmas) nm = C::kMmas;
+          const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 1024, 2);
+          const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
+          const uint64_t bd1 = make_sdesc(smem_u32(sB + s * C::kBBytes + C::kBBox), 16, 1024, 2);
+          const uint32_t sf_t = tmem_base + C::kSfCol + slot * C::kSlotCols;
+          // MMA m: compressed A bytes 32m.. (+2 descriptor units each), B box m/2 at byte
+          // 64 (m % 2) (+4 units).
+          for (int m = 0; m < nm; ++m)
+            tc_mma_mxf4nvf4_sp(acc_t, ad0 + 2 * m, ((m >> 1) ? bd1 : bd0) + 4 * (m & 1),
+                               sf_t + 32 + 2 * m, idesc, sf_t + 4 * m, sf_t + 16 + 4 * m,
+                               (kt > 0 || m > 0) ? 1u : 0u);
+          issued = true;
+          tc_commit(smem_u32(&sf_empty[slot]));
+          tc_commit(smem_u32(&empty[s]));
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&acc_full[b]));
+      }
+      if (!ok && issued) {
+        tc_commit(smem_u32(drain));
+        mbar_wait_drain(smem_u32(drain), 0, p.err_word);
+      }
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------ scale + metadata writers
+    const int q = warp & 3;
+    const int wgroup = (warp - 6) >> 2;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const int mrow_bytes = p.K / 16;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      const int row = tm * 128 + q * 32 + lane;
+      const uint8_t* ga = p.sfa + static_cast<size_t>(tm) * p.ka * 512 + lane * 16 + q * 4;
+      const uint8_t* gb = p.sfb + static_cast<size_t>(tn) * p.ka * 512 + lane * 16;
+      const uint8_t* gm = p.meta + static_cast<size_t>(row < p.M ? row : 0) * mrow_bytes;
+      for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
+        if ((it % kWriterGroups) != wgroup) continue;
+        const int s = it % C::kStages;
+        const int slot = it % C::kSfSlots;
+        int nm = p.ka - kt * C::kMmas;
+        if (nm > C::kMmas) nm = C::kMmas;
+        uint32_t va[C::kMmas], vb[16], vm[8];
+#pragma unroll
+        for (int m = 0; m < C::kMmas; ++m) {
+          const bool in = m < nm;
+          va[m] = in && tm < p.sfa_rowblocks
+                      ? __ldg(reinterpret_cast<const uint32_t*>(ga + (kt * C::kMmas + m) * 512)) : 0u;
+          uint4 x = make_uint4(0u, 0u, 0u, 0u);
+          if (in && tn < p.sfb_rowblocks)
+            x = __ldg(reinterpret_cast<const uint4*>(gb + (kt * C::kMmas + m) * 512));
+          vb[4 * m] = x.x; vb[4 * m + 1] = x.y; vb[4 * m + 2] = x.z; vb[4 * m + 3] = x.w;
+          // Metadata words 2m, 2m+1: groups 16m..16m+15 of this stage (4 bytes each).
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int off = kt * 32 + 8 * m + 4 * h;
+            vm[2 * m + h] = (in && row < p.M && off < mrow_bytes)
+                                ? __ldg(reinterpret_cast<const uint32_t*>(gm + off)) : 0u;
+          }
+        }
+        // The slot's previous use must have been consumed (and, slots <= stages, the stage's
+        // "full" barrier has finished its previous phase).
+        if (!mbar_wait(smem_u32(&sf_empty[slot]),
+                       (static_cast<uint32_t>(it / C::kSfSlots) & 1u) ^ 1u, abort_flag,
+                       p.err_word, kErrWaitSfEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sf_t = lane_base + C::kSfCol + slot * C::kSlotCols;
+#pragma unroll
+        for (int m = 0; m < C::kMmas; ++m) tmem_st_32x32b_x1(sf_t + 4 * m + q, va[m]);
+        tmem_st_32x32b_x16(sf_t + 16, vb);
+        tmem_st_32x32b_x8(sf_t + 32, vm);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&full[s]));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0};
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      const int b = local & 1;
+      const uint32_t u = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(smem_u32(&acc_full[b]), u & 1u, abort_flag, p.err_word, kErrWaitAccFull))
+        break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      const int row = tm * kBM + row_in_tile;
+      const int col_base = tn * 128;
+      e.row0 = tm * kBM + q * 32;
+      const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (b ? 128u : 0u);
+#pragma unroll
+      for (int c = 0; c < 4; c += 2) {
+        const int g[2] = {c, c + 1};
+        epi_group<2>(p, e, acc_t, g, row, col_base, 0);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
 // ---- SM-pair kernel (cta_group::2): 256 x 256 tiles ------------------------------------
 // The two CTAs of a cluster work on one 256 x 256 output tile. Each loads its own 128 rows
 // of A and its own 128 rows of B (so each SM moves half the B bytes of the one-SM kernel)
@@ -970,6 +1240,7 @@ struct DeviceState {
   int cc_major = 0, cc_minor = 0;
   bool attr_set[2] = {false, false};
   bool pair_attr_set = false;
+  bool sparse_attr_set = false;
   int pair_clusters = 0;  // co-resident SM-pair clusters of the pair kernel
   uint32_t* err_word = nullptr;
   // Workspace for canonical -> tcgen05 scale reordering (grown on demand).
@@ -1181,6 +1452,7 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   GemmParams p;
   p.sfa = sfa;
   p.sfb = sfb;
+  p.meta = nullptr;
   p.out = out;
   p.M = op.M;
   p.N = op.N;
@@ -1213,6 +1485,118 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   if (cg == 2) return launch_pair(ta, tb, tc, p, ds, s, err);
   return bn == 256 ? launch_dense<256>(ta, tb, tc, p, ds, s, err)
                    : launch_dense<128>(ta, tb, tc, p, ds, s, err);
+}
+
+// GemmMode::Sparse: A compressed ([M][K/4] kept pair bytes) + metadata ([M][K/16]) + block-32
+// scales; B dense with block-32 scales (see the sparse kernel's comment).
+bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err) {
+  DeviceState* ds = device_state(err);
+  if (!ds) return false;
+  if (ds->cc_major != 10) {
+    set_err(err, "the b200 backend needs an sm_100 device");
+    return false;
+  }
+  if (!op.a_packed || !op.b_packed || !op.a_scales || !op.b_scales || !op.a_meta) {
+    set_err(err, "sparse mode needs compressed A, its metadata (a_meta), B and both scales");
+    return false;
+  }
+  void* out = op.d ? op.d : static_cast<void*>(op.c);
+  if (!out) {
+    set_err(err, "null output pointer");
+    return false;
+  }
+  if (op.d == nullptr && op.out_dtype != OutDType::F32) {
+    set_err(err, "out_dtype BF16 needs the output in `d`");
+    return false;
+  }
+  if (op.M <= 0 || op.N <= 0 || op.K <= 0 || op.K % 128 != 0) {
+    set_err(err, "sparse mode needs positive M, N and K a multiple of 128");
+    return false;
+  }
+  if (op.cta_group == 2 || (op.tile_n != 0 && op.tile_n != 128)) {
+    set_err(err, "sparse mode runs 128 x 128 one-SM tiles (cta_group 0/1, tile_n 0/128)");
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(op.a_packed) | reinterpret_cast<uintptr_t>(op.b_packed)) & 15 ||
+      (reinterpret_cast<uintptr_t>(op.a_meta) & 3)) {
+    set_err(err, "packed operands must be 16-byte aligned and the metadata 4-byte aligned");
+    return false;
+  }
+  // Block-32 scales: the tcgen05 layout of a block-16 operand of K/2 columns.
+  const int vk = op.K / 2;
+  const uint8_t* sfa = op.a_scales;
+  const uint8_t* sfb = op.b_scales;
+  if (op.sf_layout == SfLayout::Canonical) {
+    const size_t na = sf_tcgen05_bytes(op.M, vk), nb = sf_tcgen05_bytes(op.N, vk);
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      if (ds->ws_bytes < na + nb) {
+        if (ds->ws) cudaFree(ds->ws);
+        ds->ws = nullptr;
+        ds->ws_bytes = 0;
+        if (cudaMalloc(&ds->ws, na + nb) != cudaSuccess) {
+          set_err(err, "cudaMalloc of the scale workspace failed");
+          return false;
+        }
+        ds->ws_bytes = na + nb;
+      }
+    }
+    if (!sf_to_tcgen05(op.a_scales, op.M, vk, ds->ws, s, err)) return false;
+    if (!sf_to_tcgen05(op.b_scales, op.N, vk, ds->ws + na, s, err)) return false;
+    sfa = ds->ws;
+    sfb = ds->ws + na;
+  }
+  if ((reinterpret_cast<uintptr_t>(sfa) | reinterpret_cast<uintptr_t>(sfb)) & 15) {
+    set_err(err, "tcgen05-layout scales must be 16-byte aligned");
+    return false;
+  }
+  GemmParams p;
+  p.sfa = sfa;
+  p.sfb = sfb;
+  p.meta = op.a_meta;
+  p.out = out;
+  p.M = op.M;
+  p.N = op.N;
+  p.K = op.K;
+  p.ldc = op.N;
+  p.alpha = op.a_global * op.b_global;
+  p.out_bf16 = (op.d != nullptr && op.out_dtype == OutDType::BF16) ? 1 : 0;
+  p.tiles_m = (op.M + 127) / 128;
+  p.tiles_n = (op.N + 127) / 128;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = 16;
+  p.ka = (op.K + 127) / 128;          // MMAs (and scale atoms) along K
+  p.num_kt = (op.K + 511) / 512;
+  p.sfb_rowblocks = (op.N + 127) / 128;
+  p.sfa_rowblocks = (op.M + 127) / 128;
+  p.err_word = ds->err_word;
+  CUtensorMap ta, tb, tc;
+  // Compressed A: [M][K/4] bytes, i.e. a packed operand of K/2 columns.
+  if (!cached_map(MapKey{op.a_packed, op.M, vk, 128, 0}, &ta, err)) return false;
+  if (!cached_map(MapKey{op.b_packed, op.N, op.K, 128, 0}, &tb, err)) return false;
+  std::memset(&tc, 0, sizeof(tc));
+  const int esize = p.out_bf16 ? 2 : 4;
+  p.tma_store = ((static_cast<size_t>(op.N) * esize) % 16 == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) & 15) == 0) ? 1 : 0;
+  if (p.tma_store && !cached_map(MapKey{out, op.M, op.N, 32, p.out_bf16 ? 1 : 2}, &tc, err))
+    return false;
+  if (!ds->sparse_attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_sparse_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SpCfg::kSmemBytes);
+    if (e != cudaSuccess) {
+      set_err(err, std::string("cudaFuncSetAttribute (sparse): ") + cudaGetErrorString(e));
+      return false;
+    }
+    ds->sparse_attr_set = true;
+  }
+  const int grid = p.num_tiles < ds->sms ? p.num_tiles : ds->sms;
+  gemm_sparse_kernel<<<grid, kNumThreads, SpCfg::kSmemBytes, s>>>(ta, tb, tc, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(err, std::string("sparse launch: ") + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
 }
 
 bool operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows,

@@ -284,23 +284,26 @@ void write_json(const std::string& path, const std::vector<BenchResult>& rows, c
 double run_ladder(const Dev& dev, bool print) {
   std::string err;
   double roof = 0;
-  struct Rung { int n, cg; uint32_t seed; int sustained; const char* what; };
-  const Rung rungs[] = {{128, 1, 0u, 0, "zero data, burst"},  {256, 1, 0u, 0, "zero data, burst"},
-                        {256, 2, 0u, 0, "zero data, burst"},  {256, 1, 0x5EEDu, 0, "random data, burst"},
-                        {256, 2, 0x5EEDu, 0, "random data, burst"},
-                        {256, 1, 0x5EEDu, 1, "random data, sustained ~1 s"},
-                        {256, 2, 0x5EEDu, 1, "random data, sustained ~1 s"}};
+  struct Rung { int n, cg; uint32_t seed; int sustained; int sparse; const char* what; };
+  const Rung rungs[] = {{128, 1, 0u, 0, 0, "zero data, burst"},  {256, 1, 0u, 0, 0, "zero data, burst"},
+                        {256, 2, 0u, 0, 0, "zero data, burst"},  {256, 1, 0x5EEDu, 0, 0, "random data, burst"},
+                        {256, 2, 0x5EEDu, 0, 0, "random data, burst"},
+                        {256, 1, 0x5EEDu, 1, 0, "random data, sustained ~1 s"},
+                        {256, 2, 0x5EEDu, 1, 0, "random data, sustained ~1 s"},
+                        {128, 1, 0x5EEDu, 0, 1, "sparse .sp (K 128), random data, burst"},
+                        {256, 1, 0x5EEDu, 0, 1, "sparse .sp (K 128), random data, burst"}};
   for (const Rung& r : rungs) {
     const int units = r.cg == 2 ? dev.sms / 2 : dev.sms;
-    const nvfp4b200::PeakOptions o{r.n, r.cg, units, 4096, r.sustained ? 3000 : 10, r.seed, r.sustained};
+    const nvfp4b200::PeakOptions o{r.n, r.cg, units, 4096, r.sustained ? 3000 : 10, r.seed, r.sustained, r.sparse};
     double tf = 0, mhz = 0;
     if (!nvfp4b200::peak_ladder_ex(o, &tf, &mhz, 0, &err)) {
       std::printf("peak ladder failed: %s\n", err.c_str());
       return roof;
     }
     if (print)
-      std::printf("tcgen05 kind::mxf4nvf4 block_scale %s M%d x N%d x K64, %d %s, %s: %8.1f TFLOPS at %.0f MHz\n",
-                  r.cg == 2 ? "cta_group::2" : "cta_group::1", r.cg == 2 ? 256 : 128, r.n, units,
+      std::printf("tcgen05 kind::mxf4nvf4 block_scale %s M%d x N%d x K%d, %d %s, %s: %8.1f TFLOPS at %.0f MHz\n",
+                  r.cg == 2 ? "cta_group::2" : "cta_group::1", r.cg == 2 ? 256 : 128, r.n,
+                  r.sparse ? 128 : 64, units,
                   r.cg == 2 ? "SM pairs" : "CTAs", r.what, tf, mhz);
     if (r.cg == 1 && r.n == 256 && r.seed && !r.sustained) roof = tf;
   }

@@ -15,7 +15,7 @@ inline void set_err(std::string* err, const std::string& msg) {
   if (err) *err = msg;
 }
 
-// ---- GEMM (gemm_b200.cu, gemm_sparse.cu) ---------------------------------------------
+// ---- GEMM (gemm_b200.cu, gemm_decode.cu, gemm_noalloc.cu) ---------------------------------------------
 size_t sf_tcgen05_bytes(int rows, int K);
 bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err);
 // Dense GEMM with scales already in the tcgen05 layout; `out` is op.d or op.c.
@@ -45,6 +45,19 @@ bool dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols
                 float global_scale, float* out, cudaStream_t s, std::string* err);
 bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStream_t s,
                    std::string* err);
+// Block size 16 (NVFP4, the reference's codec) or 32 (the scale block of the sparse MMA); the
+// tcgen05 scale layout of block 32 is the block-16 layout of a [rows x cols/2] operand.
+bool quantize_block(const float* src, int rows, int cols, float global_scale, int block,
+                    uint8_t* packed, uint8_t* scales, uint8_t* scales_tc, cudaStream_t s,
+                    std::string* err);
+bool dequantize_block(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                      float global_scale, int block, float* out, cudaStream_t s, std::string* err);
+// Pair-wise 2:4 sparsity of A (the sparse kernel in gemm_b200.cu): metadata [rows][K/16], prune (fp32, in place),
+// compress (packed [rows][K/2] -> values [rows][K/4]).
+bool sparse_meta(int rows, int K, uint64_t seed, uint8_t* meta, cudaStream_t s, std::string* err);
+bool sparse_prune(float* a, int rows, int K, const uint8_t* meta, cudaStream_t s, std::string* err);
+bool sparse_compress(const uint8_t* packed, int rows, int K, const uint8_t* meta, uint8_t* values,
+                     cudaStream_t s, std::string* err);
 // GPU mirror of the reference's naive FP32 oracle (src/reference.cu:9-17) with B as N x K.
 bool naive_gemm_nt(const float* A, const float* B, int M, int N, int K, float* C, cudaStream_t s,
                    std::string* err);
@@ -55,10 +68,12 @@ bool measure_bandwidth(int kind, const void* src, void* dst, const void* src2, s
 // One rung of the tcgen05 FP4 ladder. cta_group 1: `units` CTAs of M=128 x N=n MMAs; 2: `units`
 // SM pairs of M=256 x N=256. seed 0 stages zero operands, otherwise pseudo-random E2M1 bytes.
 // sustained 0: best of `reps` launches timed one by one; 1: mean of `reps` back-to-back launches.
+// sparse 1 (cta_group 1 only): tcgen05.mma.sp rungs, 128 logical K per MMA.
 struct PeakOptions {
   int n, cta_group, units, iters, reps;
   uint32_t seed;
   int sustained;
+  int sparse;
 };
 bool peak_ladder_ex(const PeakOptions& o, double* tflops, double* sm_mhz, cudaStream_t s,
                     std::string* err);

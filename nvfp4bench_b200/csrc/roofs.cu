@@ -78,7 +78,18 @@ __device__ __forceinline__ void record_clock(long long c0, uint64_t n0) {
   }
 }
 
-template <int N>
+__device__ __forceinline__ void peak_mma_sp(uint32_t d, uint64_t a, uint64_t b, uint32_t meta, uint32_t idesc,
+                                            uint32_t sfa, uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %7, 0;\n\t"
+      "tcgen05.mma.sp.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X "
+      "[%0], %1, %2, [%3], %4, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(meta), "r"(idesc), "r"(sfa), "r"(sfb), "r"(acc)
+      : "memory");
+}
+
+// SP: the sparse rung (tcgen05.mma.sp, 128 logical K per MMA: A holds the kept half).
+template <int N, bool SP = false>
 __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32_t seed, uint32_t* err_word) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -102,6 +113,16 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  if (SP) {
+    // Valid pair metadata (pairs 0 and 1 of every group) in the rows' own lanes.
+    const uint32_t lb = tbase + (static_cast<uint32_t>((threadIdx.x >> 5) * 32) << 16) + 464;
+    uint32_t v[4] = {0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u};
+    tmem_st_32x32b_x4(lb, v[0], v[1], v[2], v[3]);
+    tc_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
   if (threadIdx.x == 0) {
     const uint32_t a_s = smem_u32(smem), b_s = smem_u32(smem + kA), sf_s = smem_u32(smem + kA + kB);
     const uint32_t sfa_t = tbase + 448, sfb_t = tbase + 456;
@@ -112,7 +133,10 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int iters, uint32
     const uint64_t ad = make_sdesc(a_s, 16, 1024, 2), bd = make_sdesc(b_s, 16, 1024, 2);
     const long long c0 = clock64();
     const uint64_t n0 = globaltimer_ns();
-    for (int i = 0; i < iters; ++i) tc_mma_mxf4nvf4(tbase, ad, bd, idesc, sfa_t, sfb_t, i > 0);
+    if (SP)
+      for (int i = 0; i < iters; ++i) peak_mma_sp(tbase, ad, bd, tbase + 464, idesc | (1u << 2), sfa_t, sfb_t, i > 0);
+    else
+      for (int i = 0; i < iters; ++i) tc_mma_mxf4nvf4(tbase, ad, bd, idesc, sfa_t, sfb_t, i > 0);
     tc_commit(smem_u32(bar));
     volatile int never = 0;
     mbar_wait(smem_u32(bar), 0, &never, err_word, kErrWaitDrain);
@@ -245,8 +269,9 @@ bool peak_ladder_ex(const PeakOptions& o, double* tflops, double* sm_mhz, cudaSt
                     std::string* err) {
   const bool pair = o.cta_group == 2;
   if ((o.cta_group != 1 && !pair) || (pair ? o.n != 256 : (o.n != 128 && o.n != 256)) ||
-      o.units < 1 || o.iters < 1 || o.reps < 1 || !tflops) {
-    set_err(err, "peak: cta_group 1 (n 128 or 256) or 2 (n 256); units, iters, reps >= 1");
+      o.units < 1 || o.iters < 1 || o.reps < 1 || !tflops || (o.sparse && pair)) {
+    set_err(err, "peak: cta_group 1 (n 128 or 256, dense or sparse) or 2 (n 256, dense); "
+                 "units, iters, reps >= 1");
     return false;
   }
   uint32_t* ew = device_error_word(err);
@@ -254,7 +279,9 @@ bool peak_ladder_ex(const PeakOptions& o, double* tflops, double* sm_mhz, cudaSt
   const int kb = pair ? o.n / 2 : o.n;
   const int smem = 1024 + 128 * 128 + kb * 128 + 4096 + 64;
   void (*kern)(int, uint32_t, uint32_t*) =
-      pair ? peak_pair_kernel<256> : (o.n == 256 ? peak_kernel<256> : peak_kernel<128>);
+      pair ? peak_pair_kernel<256>
+           : o.sparse ? (o.n == 256 ? peak_kernel<256, true> : peak_kernel<128, true>)
+                      : (o.n == 256 ? peak_kernel<256> : peak_kernel<128>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_err(err, std::string("peak attr: ") + cudaGetErrorString(e));
@@ -310,7 +337,8 @@ bool peak_ladder_ex(const PeakOptions& o, double* tflops, double* sm_mhz, cudaSt
     return false;
   }
   const double m = pair ? 256.0 : 128.0;
-  *tflops = 2.0 * m * o.n * 64.0 * static_cast<double>(o.units) * o.iters / (ms_used * 1e-3) / 1e12;
+  const double k = o.sparse ? 128.0 : 64.0;   // logical K per MMA
+  *tflops = 2.0 * m * o.n * k * static_cast<double>(o.units) * o.iters / (ms_used * 1e-3) / 1e12;
   if (sm_mhz) {
     unsigned long long clk[2] = {0, 0};
     cudaMemcpyFromSymbol(clk, g_peak_clk, sizeof(clk));
@@ -321,12 +349,12 @@ bool peak_ladder_ex(const PeakOptions& o, double* tflops, double* sm_mhz, cudaSt
 
 bool peak_ladder(int n, int ctas, int iters, int reps, double* tflops, cudaStream_t s,
                  std::string* err) {
-  return peak_ladder_ex(PeakOptions{n, 1, ctas, iters, reps, 0u, 0}, tflops, nullptr, s, err);
+  return peak_ladder_ex(PeakOptions{n, 1, ctas, iters, reps, 0u, 0, 0}, tflops, nullptr, s, err);
 }
 
 bool peak_ladder_pair(int n, int clusters, int iters, int reps, double* tflops, cudaStream_t s,
                       std::string* err) {
-  return peak_ladder_ex(PeakOptions{n, 2, clusters, iters, reps, 0u, 0}, tflops, nullptr, s, err);
+  return peak_ladder_ex(PeakOptions{n, 2, clusters, iters, reps, 0u, 0, 0}, tflops, nullptr, s, err);
 }
 
 }  // namespace nvfp4b200

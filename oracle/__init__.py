@@ -65,8 +65,11 @@ def lib():
         L.orc_sf_tcgen05_bytes.restype = C.c_size_t
         L.orc_sf_tcgen05_bytes.argtypes = [C.c_int, C.c_int]
         L.orc_sf_to_tcgen05.argtypes = [_u8p, C.c_int, C.c_int, _u8p]
-        L.orc_sparse24_pairs.argtypes = [C.c_int, C.c_int, C.c_uint64, _u8p]
-        L.orc_sparse24_apply.argtypes = [_f32p, C.c_int, C.c_int, _u8p]
+        L.orc_quantize_block.argtypes = [_f32p, C.c_int, C.c_int, C.c_float, C.c_int, _u8p, _u8p]
+        L.orc_dequantize_block.argtypes = [_u8p, _u8p, C.c_int, C.c_int, C.c_float, C.c_int, _f32p]
+        L.orc_sparse_meta.argtypes = [C.c_int, C.c_int, C.c_uint64, _u8p]
+        L.orc_sparse_prune.argtypes = [_f32p, C.c_int, C.c_int, _u8p]
+        L.orc_sparse_compress.argtypes = [_u8p, C.c_int, C.c_int, _u8p, _u8p]
         L.orc_default_threads.restype = C.c_int
     return _lib
 
@@ -164,18 +167,50 @@ def sf_to_tcgen05(scales: np.ndarray, K: int) -> np.ndarray:
     return out
 
 
-def sparse24_pairs(rows: int, K: int, seed: int) -> np.ndarray:
-    out = np.empty((rows, K // 4), np.uint8)
-    lib().orc_sparse24_pairs(rows, K, seed, _p(out, _u8p))
+def quantize_block(x: np.ndarray, block: int, global_scale: float = 1.0):
+    """quantize() with `block` elements per scale: (packed [rows, cols/2], scales [rows, cols/block])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    packed = np.empty((rows, cols // 2), np.uint8)
+    scales = np.empty((rows, cols // block), np.uint8)
+    lib().orc_quantize_block(_p(x, _f32p), rows, cols, global_scale, block, _p(packed, _u8p),
+                             _p(scales, _u8p))
+    return packed, scales
+
+
+def dequantize_block(packed: np.ndarray, scales: np.ndarray, cols: int, block: int,
+                     global_scale: float = 1.0) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    scales = np.ascontiguousarray(scales, dtype=np.uint8)
+    rows = packed.shape[0]
+    out = np.empty((rows, cols), np.float32)
+    lib().orc_dequantize_block(_p(packed, _u8p), _p(scales, _u8p), rows, cols, global_scale, block,
+                               _p(out, _f32p))
     return out
 
 
-def sparse24_apply(a: np.ndarray, pairs: np.ndarray) -> np.ndarray:
+def sparse_meta(rows: int, K: int, seed: int) -> np.ndarray:
+    """Pair-wise 2:4 metadata [rows, K/16] (one nibble per group of 8 K elements)."""
+    out = np.empty((rows, K // 16), np.uint8)
+    lib().orc_sparse_meta(rows, K, seed, _p(out, _u8p))
+    return out
+
+
+def sparse_prune(a: np.ndarray, meta: np.ndarray) -> np.ndarray:
     a = np.array(a, dtype=np.float32, copy=True, order="C")
-    pairs = np.ascontiguousarray(pairs, dtype=np.uint8)
+    meta = np.ascontiguousarray(meta, dtype=np.uint8)
     rows, K = a.shape
-    lib().orc_sparse24_apply(_p(a, _f32p), rows, K, _p(pairs, _u8p))
+    lib().orc_sparse_prune(_p(a, _f32p), rows, K, _p(meta, _u8p))
     return a
+
+
+def sparse_compress(packed: np.ndarray, meta: np.ndarray, K: int) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    meta = np.ascontiguousarray(meta, dtype=np.uint8)
+    rows = packed.shape[0]
+    out = np.empty((rows, K // 4), np.uint8)
+    lib().orc_sparse_compress(_p(packed, _u8p), rows, K, _p(meta, _u8p), _p(out, _u8p))
+    return out
 
 
 def max_abs_error(got: np.ndarray, ref_: np.ndarray):

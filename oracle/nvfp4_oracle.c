@@ -97,19 +97,19 @@ uint8_t orc_e4m3_encode(float x) {
 }
 
 /* src/nvfp4.cu:62-97. amax uses std::max(amax, |x|), which ignores NaN. */
-typedef struct { const float* src; int cols; float g; uint8_t* packed; uint8_t* scales; } quant_ctx;
+typedef struct { const float* src; int cols; float g; uint8_t* packed; uint8_t* scales; int blk; } quant_ctx;
 static void quant_rows(void* p, long r0, long r1) {
   const quant_ctx* q = (const quant_ctx*)p;
   const float* src = q->src;
-  const int cols = q->cols, nb = cols / 16;
+  const int blk = q->blk, cols = q->cols, nb = cols / blk;
   const float global_scale = q->g;
   uint8_t* packed = q->packed;
   uint8_t* scales = q->scales;
   for (long r = r0; r < r1; ++r) {
     for (int b = 0; b < nb; ++b) {
-      const float* x = src + (size_t)r * cols + (size_t)b * 16;
+      const float* x = src + (size_t)r * cols + (size_t)b * blk;
       float amax = 0.0f;
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < blk; ++j) {
         float a = fabsf(x[j]);
         if (amax < a) amax = a;
       }
@@ -118,8 +118,8 @@ static void quant_rows(void* p, long r0, long r1) {
       float dec = orc_e4m3_decode(sc) * global_scale;
       if (dec <= 0.0f) dec = 1.0f;
       scales[(size_t)r * nb + b] = sc;
-      for (int j = 0; j < 16; ++j) {
-        size_t c = (size_t)b * 16 + (size_t)j;
+      for (int j = 0; j < blk; ++j) {
+        size_t c = (size_t)b * blk + (size_t)j;
         uint8_t code = orc_e2m1_quantize(x[j] / dec);
         size_t bi = ((size_t)r * cols + c) / 2;
         if ((c & 1) == 0) packed[bi] = (uint8_t)((packed[bi] & 0xF0) | (code & 0x0F));
@@ -131,18 +131,25 @@ static void quant_rows(void* p, long r0, long r1) {
 
 void orc_quantize(const float* src, int rows, int cols, float global_scale,
                   uint8_t* packed, uint8_t* scales) {
-  quant_ctx q = {src, cols, global_scale, packed, scales};
+  orc_quantize_block(src, rows, cols, global_scale, 16, packed, scales);
+}
+
+/* The same algorithm with `block` contiguous elements per scale (16 = src/nvfp4.cu; 32 = the
+ * block the sparse tensor-core MMA applies, one scale per 32 logical K elements). */
+void orc_quantize_block(const float* src, int rows, int cols, float global_scale, int block,
+                        uint8_t* packed, uint8_t* scales) {
+  quant_ctx q = {src, cols, global_scale, packed, scales, block};
   memset(packed, 0, (size_t)rows * (size_t)(cols / 2));
   parallel_range(rows, 0, quant_rows, &q);
 }
 
 /* src/nvfp4.cu:99-112 */
-typedef struct { const uint8_t* packed; const uint8_t* scales; int cols; float g; float* out; } dq_ctx;
+typedef struct { const uint8_t* packed; const uint8_t* scales; int cols; float g; float* out; int blk; } dq_ctx;
 static void dq_rows(void* p, long r0, long r1) {
   const dq_ctx* q = (const dq_ctx*)p;
   const uint8_t* packed = q->packed;
   const uint8_t* scales = q->scales;
-  const int cols = q->cols, nb = cols / 16;
+  const int blk = q->blk, cols = q->cols, nb = cols / blk;
   const float global_scale = q->g;
   float* out = q->out;
   for (long r = r0; r < r1; ++r) {
@@ -150,7 +157,7 @@ static void dq_rows(void* p, long r0, long r1) {
       size_t bi = ((size_t)r * cols + c) / 2;
       uint8_t byte = packed[bi];
       uint8_t code = (c & 1) ? (uint8_t)(byte >> 4) : (uint8_t)(byte & 0x0F);
-      float s = orc_e4m3_decode(scales[(size_t)r * nb + c / 16]) * global_scale;
+      float s = orc_e4m3_decode(scales[(size_t)r * nb + c / blk]) * global_scale;
       out[(size_t)r * cols + c] = orc_e2m1_decode(code) * s;
     }
   }
@@ -158,7 +165,12 @@ static void dq_rows(void* p, long r0, long r1) {
 
 void orc_dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
                     float global_scale, float* out) {
-  dq_ctx q = {packed, scales, cols, global_scale, out};
+  orc_dequantize_block(packed, scales, rows, cols, global_scale, 16, out);
+}
+
+void orc_dequantize_block(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                          float global_scale, int block, float* out) {
+  dq_ctx q = {packed, scales, cols, global_scale, out, block};
   parallel_range(rows, 0, dq_rows, &q);
 }
 
@@ -257,21 +269,47 @@ void orc_sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out) {
     }
 }
 
-/* Kept pairs of a 2:4 group, by index (positions inside the group of 4). */
+/* The 6 ways to keep 2 of 4: first and second kept index. */
 static const uint8_t kPairLo[6] = {0, 0, 0, 1, 1, 2};
 static const uint8_t kPairHi[6] = {1, 2, 3, 2, 3, 3};
 
-void orc_sparse24_pairs(int rows, int K, uint64_t seed, uint8_t* pair_idx) {
+
+/* Pair-wise 2:4 sparsity of A (the pattern the tcgen05 .sp kind::mxf4nvf4 MMA executes,
+ * measured on B200): each group of 8 consecutive K elements of a row is 4 element pairs, of
+ * which 2 are kept. Group i = row*K/8 + g keeps the pair combination
+ * splitmix64(seed + (i+1)*golden) % 6 of {01, 02, 03, 12, 13, 23}; its metadata nibble is
+ * first_pair | second_pair << 2, two groups per byte (even group in the low nibble). */
+void orc_sparse_meta(int rows, int K, uint64_t seed, uint8_t* meta) {
   const uint64_t g = 0x9E3779B97F4A7C15ull;
-  size_t n = (size_t)rows * (size_t)(K / 4);
-  for (size_t i = 0; i < n; ++i) pair_idx[i] = (uint8_t)(splitmix_mix(seed + (uint64_t)(i + 1) * g) % 6);
+  const size_t n = (size_t)rows * (size_t)(K / 8);
+  memset(meta, 0, n / 2);
+  for (size_t i = 0; i < n; ++i) {
+    const unsigned p = (unsigned)(splitmix_mix(seed + (uint64_t)(i + 1) * g) % 6);
+    const uint8_t nib = (uint8_t)(kPairLo[p] | (kPairHi[p] << 2));
+    meta[i / 2] |= (uint8_t)(nib << (4 * (i & 1)));
+  }
 }
 
-void orc_sparse24_apply(float* a, int rows, int K, const uint8_t* pair_idx) {
-  size_t groups = (size_t)rows * (size_t)(K / 4);
-  for (size_t gi = 0; gi < groups; ++gi) {
-    uint8_t p = pair_idx[gi];
-    for (int j = 0; j < 4; ++j)
-      if (j != kPairLo[p] && j != kPairHi[p]) a[gi * 4 + (size_t)j] = 0.0f;
+static inline uint8_t meta_nibble(const uint8_t* meta, size_t i) { return (uint8_t)((meta[i / 2] >> (4 * (i & 1))) & 0xF); }
+
+/* Zero the elements of the two dropped pairs of every group (fp32, in place). */
+void orc_sparse_prune(float* a, int rows, int K, const uint8_t* meta) {
+  const size_t n = (size_t)rows * (size_t)(K / 8);
+  for (size_t i = 0; i < n; ++i) {
+    const uint8_t nib = meta_nibble(meta, i);
+    const int p0 = nib & 3, p1 = (nib >> 2) & 3;
+    for (int pr = 0; pr < 4; ++pr)
+      if (pr != p0 && pr != p1) a[i * 8 + 2 * pr] = a[i * 8 + 2 * pr + 1] = 0.0f;
+  }
+}
+
+/* Packed [rows][K/2] -> compressed [rows][K/4]: one pair is one byte, so group i keeps bytes
+ * 4i + first and 4i + second, in that order. */
+void orc_sparse_compress(const uint8_t* packed, int rows, int K, const uint8_t* meta, uint8_t* values) {
+  const size_t n = (size_t)rows * (size_t)(K / 8);
+  for (size_t i = 0; i < n; ++i) {
+    const uint8_t nib = meta_nibble(meta, i);
+    values[2 * i] = packed[4 * i + (nib & 3)];
+    values[2 * i + 1] = packed[4 * i + ((nib >> 2) & 3)];
   }
 }

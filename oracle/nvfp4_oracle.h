@@ -35,6 +35,11 @@ void orc_quantize(const float* src, int rows, int cols, float global_scale,
 /* src/nvfp4.cu:99-112 */
 void orc_dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
                     float global_scale, float* out);
+/* orc_quantize / orc_dequantize with `block` elements per scale (16 or 32; cols % block == 0). */
+void orc_quantize_block(const float* src, int rows, int cols, float global_scale, int block,
+                        uint8_t* packed, uint8_t* scales);
+void orc_dequantize_block(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                          float global_scale, int block, float* out);
 /* src/nvfp4.cu:115-129 - splitmix64 -> uniform [-1,1) */
 void orc_make_uniform(int rows, int cols, uint64_t seed, float* out);
 
@@ -62,13 +67,14 @@ void orc_max_abs_error(const float* got, const float* ref, size_t n, double* max
 size_t orc_sf_tcgen05_bytes(int rows, int K);
 void orc_sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out);
 
-/* 2:4 structured sparsity on A rows (engine extension; the reference has no data path).
- * For each row and each group of 4 consecutive K elements, one of the 6 pairs of positions
- * is KEPT (the other two are zeroed): pair index = splitmix64(seed, row*K/4 + group) % 6.
- * Writes keep[rows*K/4] pair indices in 0..5. */
-void orc_sparse24_pairs(int rows, int K, uint64_t seed, uint8_t* pair_idx);
-/* Zero the two dropped elements of every group of 4 in place. */
-void orc_sparse24_apply(float* a, int rows, int K, const uint8_t* pair_idx);
+
+/* Pair-wise 2:4 sparsity (the pattern of the tcgen05 .sp kind::mxf4nvf4 MMA on B200): per
+ * group of 8 K elements (4 pairs) 2 pairs are kept; meta[rows*K/16] holds one nibble per
+ * group (first kept pair | second << 2; even group in the low nibble). K % 16 == 0. */
+void orc_sparse_meta(int rows, int K, uint64_t seed, uint8_t* meta);
+void orc_sparse_prune(float* a, int rows, int K, const uint8_t* meta);
+/* packed [rows][K/2] -> values [rows][K/4] (the kept pair bytes of each group, in order). */
+void orc_sparse_compress(const uint8_t* packed, int rows, int K, const uint8_t* meta, uint8_t* values);
 
 #ifdef __cplusplus
 }

@@ -42,3 +42,13 @@ def test_peak_ladder_random_data_and_clock(api, cta_group):
     with pytest.raises(api.Nvfp4Error):
         api.peak_ex(128, 2, units, 16, 1)
     assert api.device_error() == 0
+
+
+def test_peak_ladder_sparse_rung(api):
+    """The .sp rung counts 128 logical K per MMA: about twice the dense rung's FLOP rate."""
+    dense, _ = api.peak_ex(128, 1, 148, 2048, 3, seed=0x5EED)
+    sparse, _ = api.peak_ex(128, 1, 148, 2048, 3, seed=0x5EED, sparse=True)
+    assert sparse > 1.3 * dense
+    with pytest.raises(api.Nvfp4Error):
+        api.peak_ex(256, 2, 74, 16, 1, sparse=True)
+    assert api.device_error() == 0

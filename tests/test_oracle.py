@@ -132,9 +132,53 @@ def test_sf_tcgen05_layout(orc):
     assert t[(2 * ka) * 512 + 31 * 16 + 3 * 4] == 0  # row 2*128+3*32+31 = 383 >= 300
 
 
-def test_sparse24_pairs_keep_two(orc):
-    pairs = orc.sparse24_pairs(8, 64, 0x24)
-    assert pairs.max() < 6
-    a = np.ones((8, 64), np.float32)
-    z = orc.sparse24_apply(a, pairs)
-    assert np.all((z.reshape(8, 16, 4) != 0).sum(-1) == 2)
+def test_sparse_meta_keeps_two_pairs(orc):
+    """Pair-wise 2:4: every group of 8 keeps exactly 2 distinct pairs, first < second."""
+    meta = orc.sparse_meta(8, 128, 0x24)
+    nib = np.stack([meta & 0xF, meta >> 4], -1).reshape(8, 16)
+    first, second = nib & 3, nib >> 2
+    assert np.all(first < second)
+    a = np.ones((8, 128), np.float32)
+    z = orc.sparse_prune(a, meta)
+    pairs = (z.reshape(8, 16, 4, 2) != 0)
+    assert np.all(pairs.all(-1) == pairs.any(-1))          # pairs are kept or dropped whole
+    assert np.all(pairs.all(-1).sum(-1) == 2)
+    # all 6 combinations occur
+    combos = set(zip(first.ravel().tolist(), second.ravel().tolist()))
+    assert combos == {(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)}
+
+
+def test_quantize_block16_is_quantize(orc):
+    x = orc.make_uniform(16, 256, 99) * 7
+    p16, s16 = orc.quantize(x)
+    pb, sb = orc.quantize_block(x, 16)
+    assert np.array_equal(p16, pb) and np.array_equal(s16, sb)
+
+
+def test_quantize_block32_semantics(orc):
+    """Block 32: one scale per 32 elements, chosen exactly as for 16 (amax/6/g, e4m3 nearest)."""
+    x = orc.make_uniform(4, 128, 5) * 3
+    p32, s32 = orc.quantize_block(x, 32)
+    assert s32.shape == (4, 4)
+    for r in range(4):
+        for b in range(4):
+            amax = np.abs(x[r, 32 * b:32 * b + 32]).max()
+            assert s32[r, b] == orc.lib().orc_e4m3_encode(float(np.float32(amax) / np.float32(6.0)))
+    d = orc.dequantize_block(p32, s32, 128, 32)
+    assert np.abs(d - x).max() <= np.abs(x).max() / 6 * 1.01  # within one e2m1 step of each scale
+
+
+def test_sparse_compress_round_trip(orc):
+    rows, K = 16, 256
+    meta = orc.sparse_meta(rows, K, 7)
+    x = orc.sparse_prune(orc.make_uniform(rows, K, 8), meta)
+    packed, _ = orc.quantize_block(x, 32)
+    vals = orc.sparse_compress(packed, meta, K)
+    # Decompress by hand: put each kept pair byte back in its slot.
+    back = np.zeros_like(packed)
+    nib = np.stack([meta & 0xF, meta >> 4], -1).reshape(rows, K // 8)
+    for r in range(rows):
+        for g in range(K // 8):
+            back[r, 4 * g + (nib[r, g] & 3)] = vals[r, 2 * g]
+            back[r, 4 * g + (nib[r, g] >> 2)] = vals[r, 2 * g + 1]
+    assert np.array_equal(back, packed)
