@@ -38,6 +38,8 @@ CONFIGS = {
     # name: (M, N, K, out dtype, description)
     "c1": (1024, 1024, 1024, "f32", "NVFP4 GEMM 1024^3, FP32 out (BASELINE config 1)"),
     "c2": (4096, 14336, 4096, "bf16", "LLM FFN up-proj 4096x14336x4096, BF16 out (BASELINE config 2)"),
+    # BASELINE config 3's large case: N = 65536 split over the ranks (strong scaling).
+    "c3-16k": (16384, 65536, 16384, "bf16", "16384x65536x16384, BF16 out, N split over the GPUs (BASELINE config 3)"),
     # BASELINE config 4 as the tcgen05 .sp kind::mxf4nvf4 MMA executes it on B200: 2 of the 4
     # element pairs of every 8 K elements of A kept (seeded), UE4M3 scales per 32 K.
     "c4": (4096, 14336, 8192, "bf16", "pair-wise 2:4 sparse NVFP4 4096x14336x8192, BF16 out (BASELINE config 4)"),
@@ -51,6 +53,13 @@ CONFIGS = {
 }
 SEED_A, SEED_B = 1234, 1234 ^ 0xABCDEF
 SEED_SPARSE = 0x24  # pair pattern of the sparse config
+
+
+# Configs whose N is the total over all ranks (strong scaling); the others give every rank its
+# own N-wide slice of a world*N-wide weight (weak scaling).
+STRONG = {"c3-16k"}
+# The CPU baseline times a column sample of at most this many weight rows (its rate is per FLOP).
+CPU_MAX_N = 8192
 
 
 def algorithmic_bytes(M, N, K, out_bytes, sparse=False):
@@ -130,6 +139,7 @@ def cpu_reference_sample(M, N, K, target_s, threads=0):
     # Host operands of the workload's shape: uniform fill (src/nvfp4.cu:115-129) quantised and
     # dequantised by the oracle, exactly the values the reference's oracle consumes.
     a_rows = 64
+    N = min(N, CPU_MAX_N)
     a = oracle.make_uniform(a_rows, K, SEED_A)
     b = oracle.make_uniform(N, K, SEED_B)
     pa, sa = oracle.quantize(a)
@@ -197,11 +207,15 @@ def run_b200(args, rank, world, local_rank):
     out_bytes = 2 if od == "bf16" else 4
     stream = torch.cuda.current_stream()
 
-    # Operands: A replicated (same seed on every rank), B = this rank's N-slice
-    # [n0, n1) = shard_bounds(world*N, world, rank) of a world*N-wide weight, drawn with the
-    # weight seed offset by the rank.
-    n0, n1 = shard_bounds(world * N, world, rank)
-    assert n1 - n0 == N
+    # Operands: A replicated (same seed on every rank), B = this rank's N-slice [n0, n1) of a
+    # world*N-wide weight (weak scaling) or of the config's N-wide weight (strong scaling),
+    # drawn with the weight seed offset by the rank.
+    strong = args.config in STRONG
+    n_total = N if strong else world * N
+    n0, n1 = shard_bounds(n_total, world, rank)
+    N = n1 - n0
+    if max_over_ranks([N], device=dev)[0] != N:
+        raise RuntimeError("strong scaling needs equal shards: N must divide over the ranks in 128-row blocks")
     sparse = args.config == "c4"
     x = api.fill_normal(M, K, SEED_A)
     a_meta = None
@@ -381,6 +395,26 @@ def run_b200(args, rank, world, local_rank):
     if not torch.equal(hC.to(dev), C):
         raise RuntimeError("e2e output differs from the device-resident output")
 
+    gather = None
+    if args.gather and world > 1:
+        # The optional exchange: all-gather of the C column shards (NCCL), timed on its own.
+        from nvfp4bench_b200.shard import gather_columns
+        full = gather_columns(C, n_total, device=dev)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        g0.record(stream)
+        for _ in range(args.steps):
+            full = gather_columns(C, n_total, device=dev)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        g_ms = max_over_ranks([g0.elapsed_time(g1) / args.steps], device=dev)[0]
+        moved = M * N * out_bytes * (world - 1)   # bytes each rank receives
+        gather = {"ms_per_gather": g_ms, "bytes_received_per_gpu": moved,
+                  "gbs_per_gpu": moved / (g_ms * 1e-3) / 1e9,
+                  "full_shape": [int(full.shape[0]), int(full.shape[1])]}
+        del full
+
     if rank != 0:
         return 0
 
@@ -427,9 +461,10 @@ def run_b200(args, rank, world, local_rank):
     line = {
         "metric": "nvfp4_gemm_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/ue4m3->f32",
+        "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+        "dtype": "e2m1/ue4m3->f32",
         "data": "synthetic N(0,1), seeded, quantised on the GPU",
-        "config": {"workload": desc, "M": M, "N_per_gpu": N, "K": K, "out": od,
+        "config": {"workload": desc, "M": M, "N_per_gpu": N, "N_total": n_total, "K": K, "out": od,
                    "parallelism": f"N-sharded x{world}" if world > 1 else "single GPU",
                    "l2": (f"weight rotated over {len(rot)} copies ({len(rot)} x "
                           f"{(B.packed.numel() + B.scales_tc.numel()) / 1e6:.1f} MB > 3x L2), "
@@ -446,6 +481,8 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": args.steps,
         "clocks": clk,
     }
+    if gather is not None:
+        line["gather"] = gather
     print(json.dumps(line), flush=True)
     return 0
 
@@ -463,6 +500,8 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-s", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", action="store_true",
+                    help="also time an all-gather of the C column shards (N > 1)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time the device steps only (no ladder, e2e, reference-style timing or "
                          "CPU baseline): the command profiled under ncu")

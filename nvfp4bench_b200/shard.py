@@ -38,8 +38,11 @@ def gather_columns(local, n_total: int, device=None):
     M = local.shape[0]
     spans = [shard_bounds(n_total, world, r) for r in range(world)]
     width = max(n1 - n0 for n0, n1 in spans)  # collectives want equal sizes: pad, then trim
-    padded = torch.zeros((M, width), dtype=local.dtype, device=local.device)
-    padded[:, : local.shape[1]] = local
+    if local.shape[1] == width:
+        padded = local.contiguous()
+    else:
+        padded = torch.zeros((M, width), dtype=local.dtype, device=local.device)
+        padded[:, : local.shape[1]] = local
     parts = [torch.empty_like(padded) for _ in range(world)]
     dist.all_gather(parts, padded)
     return torch.cat([p[:, : n1 - n0] for p, (n0, n1) in zip(parts, spans)], dim=1)
