@@ -397,23 +397,29 @@ def run_b200(args, rank, world, local_rank):
 
     gather = None
     if args.gather and world > 1:
-        # The optional exchange: all-gather of the C column shards (NCCL), timed on its own.
-        from nvfp4bench_b200.shard import gather_columns
-        full = gather_columns(C, n_total, device=dev)
+        # The optional exchange: one NCCL all-gather of the C column shards over NVLink, then
+        # the optional copy into a row-major [M][N_total] matrix, each timed on its own.
+        from nvfp4bench_b200.shard import gather_shards, shards_to_row_major
+        shards = gather_shards(C, n_total)
+        full = shards_to_row_major(shards, n_total)
         torch.cuda.synchronize()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev3 = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         dist.barrier()
-        g0.record(stream)
+        ev3[0].record(stream)
         for _ in range(args.steps):
-            full = gather_columns(C, n_total, device=dev)
-        g1.record(stream)
+            gather_shards(C, n_total, out=shards)
+        ev3[1].record(stream)
+        for _ in range(args.steps):
+            shards_to_row_major(shards, n_total, out=full)
+        ev3[2].record(stream)
         torch.cuda.synchronize()
-        g_ms = max_over_ranks([g0.elapsed_time(g1) / args.steps], device=dev)[0]
+        g_ms, r_ms = max_over_ranks([ev3[0].elapsed_time(ev3[1]) / args.steps,
+                                     ev3[1].elapsed_time(ev3[2]) / args.steps], device=dev)
         moved = M * N * out_bytes * (world - 1)   # bytes each rank receives
-        gather = {"ms_per_gather": g_ms, "bytes_received_per_gpu": moved,
+        gather = {"ms_per_all_gather": g_ms, "bytes_received_per_gpu": moved,
                   "gbs_per_gpu": moved / (g_ms * 1e-3) / 1e9,
-                  "full_shape": [int(full.shape[0]), int(full.shape[1])]}
-        del full
+                  "ms_row_major_copy": r_ms, "full_shape": [int(full.shape[0]), int(full.shape[1])]}
+        del shards, full
 
     if rank != 0:
         return 0

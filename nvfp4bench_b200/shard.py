@@ -30,8 +30,9 @@ def max_over_ranks(values, device=None):
     return t.tolist()
 
 
-def gather_columns(local, n_total: int, device=None):
-    """All-gather of per-rank column shards [M][n1-n0] into the full [M][n_total] matrix."""
+def gather_shards(local, n_total: int, out=None):
+    """One all-gather of the per-rank column shards [M][n1-n0] into [world][M][width] (rank r's
+    shard in slot r, padded to the widest shard): the single NVLink exchange."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size()
@@ -43,6 +44,24 @@ def gather_columns(local, n_total: int, device=None):
     else:
         padded = torch.zeros((M, width), dtype=local.dtype, device=local.device)
         padded[:, : local.shape[1]] = local
-    parts = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(parts, padded)
-    return torch.cat([p[:, : n1 - n0] for p, (n0, n1) in zip(parts, spans)], dim=1)
+    if out is None:
+        out = torch.empty((world, M, width), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out.view(world * M, width), padded)
+    return out
+
+
+def shards_to_row_major(shards, n_total: int, out=None):
+    """[world][M][width] shards -> row-major [M][n_total] (the optional 2-D copy)."""
+    import torch
+    world, M, width = shards.shape
+    spans = [shard_bounds(n_total, world, r) for r in range(world)]
+    if out is None:
+        out = torch.empty((M, n_total), dtype=shards.dtype, device=shards.device)
+    for r, (n0, n1) in enumerate(spans):
+        out[:, n0:n1].copy_(shards[r, :, : n1 - n0])
+    return out
+
+
+def gather_columns(local, n_total: int, device=None):
+    """All-gather of per-rank column shards [M][n1-n0] into the full [M][n_total] matrix."""
+    return shards_to_row_major(gather_shards(local, n_total), n_total)
