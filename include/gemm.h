@@ -28,7 +28,7 @@
 #include "common.h"
 
 enum class SfLayout { Canonical = 0, Tcgen05 = 1 };
-enum class OutDType { F32 = 0, BF16 = 1 };
+enum class OutDType { F32 = 0, BF16 = 1, NVFP4 = 2 };
 
 // src/gemm.h:13-23, extended with defaulted fields (a reference-style initialisation of
 // the first ten fields keeps its meaning).
@@ -49,6 +49,11 @@ struct Nvfp4DeviceOperands {
   const uint8_t* a_meta = nullptr;   // 2:4 metadata (GemmMode::Sparse)
   int cta_group = 0;                 // 0 = heuristic, 1 = one-SM tiles, 2 = SM-pair tiles
   int tile_n = 0;                    // 0 = heuristic, else 64/128/256
+  // NVFP4 output (out_dtype NVFP4): `d` = packed [M][N/2], `d_scales` in d_sf_layout, quantised
+  // exactly as quantize_to_nvfp4 (src/nvfp4.cu:62-97) with global scale d_global.
+  uint8_t* d_scales = nullptr;
+  float d_global = 1.0f;
+  SfLayout d_sf_layout = SfLayout::Canonical;
 };
 
 // src/gemm.h:25-29. Each backend returns true on success; on failure it sets *err (which

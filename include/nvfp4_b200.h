@@ -29,7 +29,7 @@ enum {
 /* GemmMode / SfLayout / OutDType values (include/gemm.h). */
 enum { NVFP4_MODE_DENSE = 0, NVFP4_MODE_SPARSE24 = 1 };
 enum { NVFP4_SF_CANONICAL = 0, NVFP4_SF_TCGEN05 = 1 };
-enum { NVFP4_OUT_F32 = 0, NVFP4_OUT_BF16 = 1 };
+enum { NVFP4_OUT_F32 = 0, NVFP4_OUT_BF16 = 1, NVFP4_OUT_NVFP4 = 2 };
 
 /* Flat form of Nvfp4DeviceOperands (include/gemm.h; reference src/gemm.h:13-23). */
 typedef struct Nvfp4GemmArgs {
@@ -47,6 +47,13 @@ typedef struct Nvfp4GemmArgs {
   const void* a_meta;   /* 2:4 metadata, mode == NVFP4_MODE_SPARSE24 only */
   int cta_group;        /* 0 = heuristic, 1 or 2 */
   int tile_n;           /* 0 = heuristic, else 64, 128 or 256 */
+  /* out_dtype NVFP4_OUT_NVFP4: c = packed [M][N/2] (N % 32 == 0), c_scales = its UE4M3 scales
+   * in c_sf_layout (canonical [M][N/16] or tcgen05, nvfp4_b200_sf_tcgen05_bytes(M, N)),
+   * quantised from alpha*acc exactly as quantize_to_nvfp4 (src/nvfp4.cu:62-97) with global
+   * scale c_global: the next layer's A operand, byte-identical to quantising the FP32 output. */
+  void* c_scales;
+  float c_global;
+  int c_sf_layout;
 } Nvfp4GemmArgs;
 
 /* Replaces launch_gemm(KernelKind::Custom, op, s, err) - src/gemm.h:31-40 and the

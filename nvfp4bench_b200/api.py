@@ -21,7 +21,7 @@ LIB_PATH = os.environ.get("NVFP4_B200_LIB", _build.LIB)
 
 MODE_DENSE, MODE_SPARSE24 = 0, 1
 SF_CANONICAL, SF_TCGEN05 = 0, 1
-OUT_F32, OUT_BF16 = 0, 1
+OUT_F32, OUT_BF16, OUT_NVFP4 = 0, 1, 2
 
 # Every symbol include/nvfp4_b200.h declares (checked by the CPU tests).
 EXPORTED = [
@@ -52,6 +52,7 @@ class GemmArgs(C.Structure):
         ("c", C.c_void_p), ("M", C.c_int), ("N", C.c_int), ("K", C.c_int),
         ("mode", C.c_int), ("sf_layout", C.c_int), ("out_dtype", C.c_int),
         ("a_meta", C.c_void_p), ("cta_group", C.c_int), ("tile_n", C.c_int),
+        ("c_scales", C.c_void_p), ("c_global", C.c_float), ("c_sf_layout", C.c_int),
     ]
 
 
@@ -122,31 +123,40 @@ def _ptr(t: Optional[torch.Tensor]):
 
 
 # ---- entry points -------------------------------------------------------------------------
+def _out_kind(out, out_scales):
+    if out.dtype == torch.float32:
+        return OUT_F32
+    if out.dtype == torch.bfloat16:
+        return OUT_BF16
+    if out.dtype == torch.uint8 and out_scales is not None:
+        return OUT_NVFP4
+    raise ValueError("out must be float32, bfloat16, or uint8 packed NVFP4 with out_scales")
+
+
 def gemm(a_packed, a_scales, b_packed, b_scales, M: int, N: int, K: int, out: torch.Tensor,
          a_global: float = 1.0, b_global: float = 1.0, sf_layout: int = SF_TCGEN05,
          mode: int = MODE_DENSE, a_meta=None, cta_group: int = 0, tile_n: int = 0,
+         out_scales=None, out_global: float = 1.0, out_sf_layout: int = SF_CANONICAL,
          stream=None) -> torch.Tensor:
-    """D = (a_global*b_global) * A @ B^T into `out` (float32 or bfloat16, [M, N])."""
-    if out.dtype == torch.float32:
-        od = OUT_F32
-    elif out.dtype == torch.bfloat16:
-        od = OUT_BF16
-    else:
-        raise ValueError("out must be float32 or bfloat16")
-    args = GemmArgs(_ptr(a_packed), _ptr(a_scales), a_global, _ptr(b_packed), _ptr(b_scales),
-                    b_global, _ptr(out), M, N, K, mode, sf_layout, od, _ptr(a_meta), cta_group,
-                    tile_n)
+    """D = (a_global*b_global) * A @ B^T into `out`: float32 or bfloat16 [M, N], or packed NVFP4
+    uint8 [M, N/2] with `out_scales` (canonical [M, N/16] or tcgen05 layout) and `out_global`."""
+    args = gemm_args(a_packed, a_scales, b_packed, b_scales, M, N, K, out, a_global=a_global,
+                     b_global=b_global, sf_layout=sf_layout, mode=mode, a_meta=a_meta,
+                     cta_group=cta_group, tile_n=tile_n, out_scales=out_scales,
+                     out_global=out_global, out_sf_layout=out_sf_layout)
     _call(lib().nvfp4_b200_gemm, C.byref(args), _stream(stream))
     return out
 
 
 def gemm_args(a_packed, a_scales, b_packed, b_scales, M, N, K, out, **kw) -> GemmArgs:
     """Prebuilt argument block for repeated launches (see launch())."""
-    od = OUT_BF16 if out.dtype == torch.bfloat16 else OUT_F32
+    od = _out_kind(out, kw.get("out_scales"))
     return GemmArgs(_ptr(a_packed), _ptr(a_scales), kw.get("a_global", 1.0), _ptr(b_packed),
                     _ptr(b_scales), kw.get("b_global", 1.0), _ptr(out), M, N, K,
                     kw.get("mode", MODE_DENSE), kw.get("sf_layout", SF_TCGEN05), od,
-                    _ptr(kw.get("a_meta")), kw.get("cta_group", 0), kw.get("tile_n", 0))
+                    _ptr(kw.get("a_meta")), kw.get("cta_group", 0), kw.get("tile_n", 0),
+                    _ptr(kw.get("out_scales")), kw.get("out_global", 1.0),
+                    kw.get("out_sf_layout", SF_CANONICAL))
 
 
 def launch(args: GemmArgs, stream=None) -> None:

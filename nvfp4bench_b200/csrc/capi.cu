@@ -72,11 +72,21 @@ int nvfp4_b200_gemm(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errl
     return fail(NVFP4_B200_EINVAL, "unknown mode", err, errlen);
   if (a->sf_layout != NVFP4_SF_CANONICAL && a->sf_layout != NVFP4_SF_TCGEN05)
     return fail(NVFP4_B200_EINVAL, "unknown sf_layout", err, errlen);
-  if (a->out_dtype != NVFP4_OUT_F32 && a->out_dtype != NVFP4_OUT_BF16)
+  if (a->out_dtype != NVFP4_OUT_F32 && a->out_dtype != NVFP4_OUT_BF16 &&
+      a->out_dtype != NVFP4_OUT_NVFP4)
     return fail(NVFP4_B200_EINVAL, "unknown out_dtype", err, errlen);
   op.mode = a->mode == NVFP4_MODE_SPARSE24 ? GemmMode::Sparse : GemmMode::Dense;
   op.sf_layout = a->sf_layout == NVFP4_SF_TCGEN05 ? SfLayout::Tcgen05 : SfLayout::Canonical;
-  op.out_dtype = a->out_dtype == NVFP4_OUT_BF16 ? OutDType::BF16 : OutDType::F32;
+  op.out_dtype = a->out_dtype == NVFP4_OUT_BF16    ? OutDType::BF16
+                 : a->out_dtype == NVFP4_OUT_NVFP4 ? OutDType::NVFP4
+                                                   : OutDType::F32;
+  if (op.out_dtype == OutDType::NVFP4) {
+    if (a->c_sf_layout != NVFP4_SF_CANONICAL && a->c_sf_layout != NVFP4_SF_TCGEN05)
+      return fail(NVFP4_B200_EINVAL, "unknown c_sf_layout", err, errlen);
+    op.d_scales = static_cast<uint8_t*>(a->c_scales);
+    op.d_global = a->c_global;
+    op.d_sf_layout = a->c_sf_layout == NVFP4_SF_TCGEN05 ? SfLayout::Tcgen05 : SfLayout::Canonical;
+  }
   op.d = a->c;
   op.a_meta = static_cast<const uint8_t*>(a->a_meta);
   op.cta_group = a->cta_group;

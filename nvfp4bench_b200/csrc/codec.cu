@@ -17,63 +17,11 @@
 
 #include <string>
 
+#include "codec_dev.cuh"
 #include "internal.h"
 
 namespace nvfp4b200 {
 namespace {
-
-constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;
-
-__device__ __forceinline__ uint64_t splitmix_mix(uint64_t z) {
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
-// src/nvfp4.cu:34-45 for positive codes, built from the bit pattern (exact).
-__device__ __forceinline__ float e4m3_decode_pos(int c) {
-  const int e = (c >> 3) & 0xF, m = c & 7;
-  if (e == 0) return __fmul_rn(static_cast<float>(m), 0.001953125f);  // m/8 * 2^-6
-  return __int_as_float(((e + 120) << 23) | (m << 20));                 // (1+m/8) * 2^(e-7)
-}
-__device__ __forceinline__ float e4m3_decode_dev(uint8_t code) {
-  const float v = e4m3_decode_pos(code & 0x7F);
-  return (code & 0x80) ? -v : v;
-}
-
-__device__ __forceinline__ uint8_t e4m3_encode_dev(float x) {
-  if (!(x > 0.0f)) return 0;  // x <= 0 -> 0; NaN -> 0 (no error ever compares smaller)
-  if (448.0f < x) x = 448.0f;
-  int lo = 1, hi = 126;       // dec(0) = 0 < x and dec(126) = 448 >= x
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (e4m3_decode_pos(mid) >= x) hi = mid; else lo = mid + 1;
-  }
-  const float eh = fabsf(__fsub_rn(e4m3_decode_pos(hi), x));
-  const float el = fabsf(__fsub_rn(e4m3_decode_pos(hi - 1), x));
-  return static_cast<uint8_t>(eh < el ? hi : hi - 1);
-}
-
-// src/nvfp4.cu:18-29, verbatim in structure.
-__device__ __forceinline__ uint8_t e2m1_quantize_dev(float x) {
-  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
-  const uint8_t sign = (x < 0.0f) ? 0x8 : 0x0;
-  const float a = fabsf(x);
-  int best = 0;
-  float best_err = fabsf(__fsub_rn(a, mag[0]));
-#pragma unroll
-  for (int i = 1; i < 8; ++i) {
-    const float e = fabsf(__fsub_rn(a, mag[i]));
-    if (e < best_err) { best_err = e; best = i; }
-  }
-  return static_cast<uint8_t>(sign | best);
-}
-
-__device__ __forceinline__ float e2m1_decode_dev(uint8_t code) {
-  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
-  const float m = mag[code & 7];
-  return (code & 8) ? -m : m;
-}
 
 __global__ void fill_uniform_kernel(float* __restrict__ out, size_t n, uint64_t x0) {
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n;

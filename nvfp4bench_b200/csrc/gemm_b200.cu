@@ -57,6 +57,7 @@
 
 #include "gemm.h"
 #include "internal.h"
+#include "codec_dev.cuh"
 #include "ptx.cuh"
 
 namespace nvfp4b200 {
@@ -117,6 +118,11 @@ struct GemmParams {
   int group_m;
   int ka;               // scale atoms along K = ceil(K/64) (sparse: ceil(K/128))
   const uint8_t* meta;  // sparse: pair metadata [M][K/16]
+  int out_nvfp4;        // 1: `out` is packed NVFP4 [M][N/2] with scales out_sf
+  uint8_t* out_sf;
+  float out_g;          // its global scale
+  int out_sf_tc;        // out_sf in the tcgen05 layout (else canonical [M][N/16])
+  int out_ka;           // tcgen05 scale atoms per 128-row block of the output = ceil(N/64)
   int num_kt;           // K-stages = ceil(K/256)
   int sfb_rowblocks;    // ceil(N/128)
   int sfa_rowblocks;    // ceil(M/128)
@@ -186,6 +192,33 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
   }
 }
 
+// NVFP4 output: the chunk's two 16-column blocks of row `row` quantised exactly as
+// quantize_to_nvfp4 (src/nvfp4.cu:62-97, shared device code): 16 packed bytes and 2 scale
+// bytes. N % 32 == 0, so a chunk is wholly inside or outside the matrix.
+__device__ __forceinline__ void store_chunk_nvfp4(const GemmParams& p, const uint32_t (&r)[32], int row,
+                                                  int col0) {
+  if (row >= p.M || col0 >= p.N) return;
+  float x0[16], x1[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    x0[j] = __fmul_rn(__uint_as_float(r[j]), p.alpha);
+    x1[j] = __fmul_rn(__uint_as_float(r[16 + j]), p.alpha);
+  }
+  uint32_t a0, a1, b0, b1;
+  const uint32_t s0 = quantize16_dev(x0, p.out_g, a0, a1);
+  const uint32_t s1 = quantize16_dev(x1, p.out_g, b0, b1);
+  uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
+  *reinterpret_cast<uint4*>(out + (static_cast<size_t>(row) * p.N + col0) / 2) = make_uint4(a0, a1, b0, b1);
+  const int s = col0 / 16;
+  size_t off;
+  if (p.out_sf_tc)
+    off = (static_cast<size_t>(row / 128) * p.out_ka + s / 4) * 512 + (row % 32) * 16 +
+          ((row / 32) % 4) * 4 + (s % 4);
+  else
+    off = static_cast<size_t>(row) * (p.N / 16) + s;
+  *reinterpret_cast<uint16_t*>(p.out_sf + off) = static_cast<uint16_t>(s0 | (s1 << 8));
+}
+
 // Per-warp epilogue state for the TMA-store path: two 4 KB staging buffers used in turn.
 struct EpiStage {
   uint8_t* buf;        // this warp's two buffers
@@ -249,7 +282,8 @@ __device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint
   }
 #pragma unroll
   for (int g = 0; g < CNT; ++g) {
-    if (p.tma_store) stage_chunk(p, e, r[g], col_base + cs[g] * 32);
+    if (p.out_nvfp4) store_chunk_nvfp4(p, r[g], row, col_base + cs[g] * 32);
+    else if (p.tma_store) stage_chunk(p, e, r[g], col_base + cs[g] * 32);
     else store_chunk(p, r[g], row, col_base + cs[g] * 32);
   }
 }
@@ -1417,6 +1451,28 @@ bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err)
   return gemm_dense_tc(op, sfa, sfb, out, s, err);
 }
 
+// NVFP4 output parameters (and the zeroed padding of a tcgen05-layout scale buffer); also
+// turns the TMA-store path off, which writes FP32/BF16 tiles only.
+bool setup_nvfp4_out(const Nvfp4DeviceOperands& op, GemmParams& p, cudaStream_t s, std::string* err) {
+  p.out_nvfp4 = op.out_dtype == OutDType::NVFP4 ? 1 : 0;
+  p.out_sf = op.d_scales;
+  p.out_g = op.d_global;
+  p.out_sf_tc = op.d_sf_layout == SfLayout::Tcgen05 ? 1 : 0;
+  p.out_ka = (op.N + 63) / 64;
+  if (!p.out_nvfp4) return true;
+  if (!op.d || !op.d_scales || op.N % 32 != 0 || (reinterpret_cast<uintptr_t>(op.d) & 15) ||
+      (reinterpret_cast<uintptr_t>(op.d_scales) & 1)) {
+    set_err(err, "NVFP4 output needs d (16-byte aligned) and d_scales, and N a multiple of 32");
+    return false;
+  }
+  if (p.out_sf_tc && op.M % 128 != 0 &&
+      cudaMemsetAsync(op.d_scales, 0, sf_tcgen05_bytes(op.M, op.N), s) != cudaSuccess) {
+    set_err(err, "cudaMemsetAsync of the output scale buffer failed");
+    return false;
+  }
+  return true;
+}
+
 bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb,
                    void* out, cudaStream_t s, std::string* err) {
   DeviceState* ds = device_state(err);
@@ -1425,7 +1481,7 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   // the MMA's 128-row side, one CTA per SM, split-K over a cluster when the weight has fewer
   // 128-row tiles than there are SMs). An explicit tile shape or SM grouping selects the
   // general kernel.
-  if (op.M <= 128 && op.cta_group == 0 && op.tile_n == 0)
+  if (op.M <= 128 && op.cta_group == 0 && op.tile_n == 0 && op.out_dtype != OutDType::NVFP4)
     return gemm_decode(op, sfa, sfb, out, s, err);
   int bn = op.tile_n;
   const int tiles_m = (op.M + kBM - 1) / kBM;
@@ -1470,13 +1526,14 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   p.sfa_rowblocks = (op.M + 127) / 128;
   p.group_m = cg == 2 ? 8 : 16;
   p.err_word = ds->err_word;
+  if (!setup_nvfp4_out(op, p, s, err)) return false;
   CUtensorMap ta, tb;
   if (!cached_map(MapKey{op.a_packed, op.M, op.K, kBM, 0}, &ta, err)) return false;
   if (!cached_map(MapKey{op.b_packed, op.N, op.K, cg == 2 ? 128 : bn, 0}, &tb, err)) return false;
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   const int esize = p.out_bf16 ? 2 : 4;
-  p.tma_store = ((static_cast<size_t>(op.N) * esize) % 16 == 0 &&
+  p.tma_store = (!p.out_nvfp4 && (static_cast<size_t>(op.N) * esize) % 16 == 0 &&
                  (reinterpret_cast<uintptr_t>(out) & 15) == 0)
                     ? 1 : 0;
   if (p.tma_store &&
@@ -1570,13 +1627,14 @@ bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err
   p.sfb_rowblocks = (op.N + 127) / 128;
   p.sfa_rowblocks = (op.M + 127) / 128;
   p.err_word = ds->err_word;
+  if (!setup_nvfp4_out(op, p, s, err)) return false;
   CUtensorMap ta, tb, tc;
   // Compressed A: [M][K/4] bytes, i.e. a packed operand of K/2 columns.
   if (!cached_map(MapKey{op.a_packed, op.M, vk, 128, 0}, &ta, err)) return false;
   if (!cached_map(MapKey{op.b_packed, op.N, op.K, 128, 0}, &tb, err)) return false;
   std::memset(&tc, 0, sizeof(tc));
   const int esize = p.out_bf16 ? 2 : 4;
-  p.tma_store = ((static_cast<size_t>(op.N) * esize) % 16 == 0 &&
+  p.tma_store = (!p.out_nvfp4 && (static_cast<size_t>(op.N) * esize) % 16 == 0 &&
                  (reinterpret_cast<uintptr_t>(out) & 15) == 0) ? 1 : 0;
   if (p.tma_store && !cached_map(MapKey{out, op.M, op.N, 32, p.out_bf16 ? 1 : 2}, &tc, err))
     return false;
