@@ -77,28 +77,48 @@ bool eq(const char* a, const char* b) { return std::strcmp(a, b) == 0; }
   } while (0)
 
 struct Operand {
-  uint8_t* packed = nullptr;
+  uint8_t* packed = nullptr;     // dense [rows][K/2]; sparse A: kept values [rows][K/4]
   uint8_t* scales = nullptr;
   uint8_t* scales_tc = nullptr;
+  uint8_t* meta = nullptr;       // sparse A: pair metadata [rows][K/16]
   void free() {
     cudaFree(packed);
     cudaFree(scales);
     cudaFree(scales_tc);
+    cudaFree(meta);
   }
 };
 
-Operand make_operand(int rows, int K, uint64_t seed, bool normal, float* keep_dequant) {
+// Sparse mode: block 32 scales for A and B (the sparse MMA's block); sparse_a: prune A with a
+// seeded pair pattern and compress it (the dequantised copy keeps the pruned dense values).
+Operand make_operand(int rows, int K, uint64_t seed, bool normal, float* keep_dequant,
+                     bool sparse_mode = false, bool sparse_a = false) {
   Operand o;
   float* x = nullptr;
   CK(cudaMalloc(&x, sizeof(float) * size_t(rows) * K));
   std::string err;
   bool ok = normal ? nvfp4b200::fill_normal(x, size_t(rows) * K, seed, 0, &err)
                    : nvfp4b200::fill_uniform(x, size_t(rows) * K, seed, 0, &err);
+  const int block = sparse_mode ? 32 : 16;
+  if (ok && sparse_a) {
+    CK(cudaMalloc(&o.meta, size_t(rows) * K / 16));
+    ok = nvfp4b200::sparse_meta(rows, K, 0x24, o.meta, 0, &err) &&
+         nvfp4b200::sparse_prune(x, rows, K, o.meta, 0, &err);
+  }
   CK(cudaMalloc(&o.packed, size_t(rows) * K / 2));
-  CK(cudaMalloc(&o.scales, size_t(rows) * K / 16));
-  CK(cudaMalloc(&o.scales_tc, nvfp4b200::sf_tcgen05_bytes(rows, K)));
-  ok = ok && nvfp4b200::quantize(x, rows, K, 1.0f, o.packed, o.scales, o.scales_tc, 0, &err);
-  if (ok && keep_dequant) ok = nvfp4b200::dequantize(o.packed, o.scales, rows, K, 1.0f, keep_dequant, 0, &err);
+  CK(cudaMalloc(&o.scales, size_t(rows) * K / block));
+  CK(cudaMalloc(&o.scales_tc, nvfp4b200::sf_tcgen05_bytes(rows, block == 16 ? K : K / 2)));
+  ok = ok && nvfp4b200::quantize_block(x, rows, K, 1.0f, block, o.packed, o.scales, o.scales_tc, 0, &err);
+  if (ok && keep_dequant)
+    ok = nvfp4b200::dequantize_block(o.packed, o.scales, rows, K, 1.0f, block, keep_dequant, 0, &err);
+  if (ok && sparse_a) {
+    uint8_t* vals = nullptr;
+    CK(cudaMalloc(&vals, size_t(rows) * K / 4));
+    ok = nvfp4b200::sparse_compress(o.packed, rows, K, o.meta, vals, 0, &err);
+    CK(cudaDeviceSynchronize());
+    cudaFree(o.packed);
+    o.packed = vals;
+  }
   if (!ok) {
     std::fprintf(stderr, "operand set-up failed: %s\n", err.c_str());
     std::exit(1);
@@ -117,8 +137,9 @@ BenchResult run_bench(KernelKind kind, const GemmProblem& prob, const Dev& dev, 
     CK(cudaMalloc(&adq, sizeof(float) * size_t(M) * K));
     CK(cudaMalloc(&bdq, sizeof(float) * size_t(N) * K));
   }
-  Operand A = make_operand(M, K, cfg.seed, cfg.normal, adq);
-  Operand B = make_operand(N, K, cfg.seed ^ 0xABCDEF, cfg.normal, bdq);  // src/bench.cu:29-30
+  const bool sparse = prob.mode == GemmMode::Sparse;
+  Operand A = make_operand(M, K, cfg.seed, cfg.normal, adq, sparse, sparse);
+  Operand B = make_operand(N, K, cfg.seed ^ 0xABCDEF, cfg.normal, bdq, sparse);  // src/bench.cu:29-30
   void* c = nullptr;
   const size_t esize = cfg.bf16 ? 2 : 4;
   CK(cudaMalloc(&c, esize * size_t(M) * N));
@@ -132,6 +153,7 @@ BenchResult run_bench(KernelKind kind, const GemmProblem& prob, const Dev& dev, 
   op.N = N;
   op.K = K;
   op.mode = prob.mode;
+  op.a_meta = A.meta;
   op.sf_layout = cfg.tcgen05_sf ? SfLayout::Tcgen05 : SfLayout::Canonical;
   op.out_dtype = cfg.bf16 ? OutDType::BF16 : OutDType::F32;
   op.d = c;
@@ -168,8 +190,10 @@ BenchResult run_bench(KernelKind kind, const GemmProblem& prob, const Dev& dev, 
     r.tflops = gemm_flops(prob) / (r.median_ms * 1e-3) / 1e12;
     r.peak_tflops = gemm_flops(prob) / (r.min_ms * 1e-3) / 1e12;
     if (dev.peak_tflops > 0) r.pct_dense_peak = 100.0 * r.peak_tflops / dev.peak_tflops;
-    r.algorithmic_bytes = double(M) * K / 2 + double(M) * K / 16 + double(N) * K / 2 +
-                          double(N) * K / 16 + double(M) * N * esize;
+    r.algorithmic_bytes = sparse ? double(M) * K / 4 + double(M) * K / 16 + double(M) * K / 32 +
+                                       double(N) * K / 2 + double(N) * K / 32 + double(M) * N * esize
+                                 : double(M) * K / 2 + double(M) * K / 16 + double(N) * K / 2 +
+                                       double(N) * K / 16 + double(M) * N * esize;
     r.gbs = r.algorithmic_bytes / (r.min_ms * 1e-3) / 1e9;
     uint32_t* ew = nvfp4b200::device_error_word(&err);
     uint32_t word = 0;

@@ -24,6 +24,8 @@ def _run(args, tmp_path=None):
     ["--m", "300", "--n", "520", "--k", "288", "--dist", "uniform"],
     ["--m", "16", "--n", "4096", "--k", "14336", "--out", "bf16"],
     ["--m", "1024", "--n", "2048", "--k", "1024", "--cta-group", "2"],
+    ["--m", "512", "--n", "640", "--k", "1024", "--mode", "sparse"],
+    ["--m", "300", "--n", "384", "--k", "640", "--mode", "sparse", "--out", "bf16", "--sf", "canonical"],
 ])
 def test_cli_validate(args, tmp_path):
     js = tmp_path / "r.json"
