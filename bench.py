@@ -275,8 +275,21 @@ def run_b200(args, rank, world, local_rank):
                                      sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
                                      cta_group=args.cta_group))
     step_no = [0]
+    # --quantize-a (decode): every step first quantises the fp32 activations A into the tcgen05
+    # layout the GEMM reads (the per-call cost of a real decode layer), then runs the GEMM.
+    xa = None
+    if args.quantize_a:
+        if sparse:
+            raise SystemExit("--quantize-a applies to dense configs")
+        xa = api.fill_normal(M, K, SEED_A)
+        qa = api.lib()
+        import ctypes as _C
+        qa_args = (xa.data_ptr(), M, K, _C.c_float(1.0), A.packed.data_ptr(), None,
+                   A.scales_tc.data_ptr())
 
     def step():
+        if xa is not None:
+            api._call(qa.nvfp4_b200_quantize, *qa_args, api._stream(None))
         api.launch(rot[step_no[0] % len(rot)])
         step_no[0] += 1
 
@@ -477,14 +490,15 @@ def run_b200(args, rank, world, local_rank):
                           "no flush; host enqueue ahead of a GPU spin; per-step CUDA events"
                           if decode else
                           "flushed (256 MiB write) before every step; per-step CUDA events"),
-                   "tile_n": args.tile_n or "auto", "sf_layout": "tcgen05"},
+                   "tile_n": args.tile_n or "auto", "sf_layout": "tcgen05",
+                   "step": ("quantise fp32 A (GPU) + GEMM" if args.quantize_a else "GEMM")},
         "burst_tflops": burst_tf, "sustained_tflops": sust_tf,
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if args.quantize_a else 1),
         "clocks": clk,
     }
     if gather is not None:
@@ -506,6 +520,8 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-s", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quantize-a", action="store_true",
+                    help="each step quantises fp32 A on the GPU before the GEMM (decode layers)")
     ap.add_argument("--gather", action="store_true",
                     help="also time an all-gather of the C column shards (N > 1)")
     ap.add_argument("--kernel-only", action="store_true",

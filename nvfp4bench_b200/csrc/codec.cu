@@ -53,6 +53,11 @@ template <int BLK>
 __global__ void quantize_kernel(const float* __restrict__ src, int rows, int cols, float g,
                                 uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
                                 uint8_t* __restrict__ scales_tc, int ka) {
+  // Launched with programmatic stream serialization: read the source only once the previous
+  // kernel has completed, and let the next kernel (typically the GEMM reading these bytes,
+  // which waits for this grid the same way) start its set-up now.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int nb = cols / BLK;
   const size_t nblocks = static_cast<size_t>(rows) * nb;
   for (size_t blk = blockIdx.x * size_t(blockDim.x) + threadIdx.x; blk < nblocks;
@@ -251,12 +256,24 @@ bool quantize_block(const float* src, int rows, int cols, float global_scale, in
     }
   }
   const int ka = (vcols + 63) / 64;
-  if (block == 16)
-    quantize_kernel<16><<<grid_for(nblocks, 256), 256, 0, s>>>(src, rows, cols, global_scale, packed,
-                                                              scales, scales_tc, ka);
-  else
-    quantize_kernel<32><<<grid_for(nblocks, 256), 256, 0, s>>>(src, rows, cols, global_scale, packed,
-                                                              scales, scales_tc, ka);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid_for(nblocks, 256), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = block == 16
+      ? cudaLaunchKernelEx(&cfg, quantize_kernel<16>, src, rows, cols, global_scale, packed, scales,
+                           scales_tc, ka)
+      : cudaLaunchKernelEx(&cfg, quantize_kernel<32>, src, rows, cols, global_scale, packed, scales,
+                           scales_tc, ka);
+  if (e != cudaSuccess) {
+    set_err(err, std::string("quantize launch: ") + cudaGetErrorString(e));
+    return false;
+  }
   return check_launch("quantize", err);
 }
 
