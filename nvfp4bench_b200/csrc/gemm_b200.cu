@@ -78,9 +78,11 @@ constexpr int kSfbOff = 16;
 #define NVFP4_SF_SLOTS 2
 #endif
 
-template <int BN>
+// SP: the sparse variant (tcgen05.mma.sp, pair-wise 2:4 A): a stage is 256 logical K, A
+// compressed to 64 bytes per row (one 64-byte-swizzled TMA box), two sparse MMAs of N = BN.
+template <int BN, bool SP = false>
 struct Cfg {
-  static constexpr int kABytes = kBM * kBKBytes;                 // 16 KB
+  static constexpr int kABytes = kBM * (SP ? 64 : kBKBytes);     // 16 KB (8 KB compressed)
   static constexpr int kBBytes = BN * kBKBytes;                  // 16 / 32 KB
   static constexpr int kStageBytes = kABytes + kBBytes;          // scales bypass smem
   static constexpr int kStages = (BN == 256) ? 4 : 6;
@@ -322,12 +324,24 @@ __device__ __forceinline__ void drain_overlapped(const GemmParams& p, EpiStage& 
   }
 }
 
-template <int BN>
+__device__ __forceinline__ void tc_mma_mxf4nvf4_sp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                   uint32_t meta_tmem, uint32_t idesc, uint32_t sfa_tmem,
+                                                   uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %7, 0;\n\t"
+      "tcgen05.mma.sp.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X "
+      "[%0], %1, %2, [%3], %4, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem),
+      "r"(accumulate)
+      : "memory");
+}
+
+template <int BN, bool SP = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_mxf4nvf4_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, SP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -394,7 +408,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           const uint32_t fb = smem_u32(&full[s]);
           mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes);
-          tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * kBKBytes, m0, fb);
+          tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * (SP ? 64 : kBKBytes), m0, fb);
           tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes, n0, fb);
         }
       }
@@ -412,7 +426,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc_mxf4nvf4(kBM, BN);
+      const uint32_t idesc = make_idesc_mxf4nvf4(kBM, BN) | (SP ? (1u << 2) : 0u);  // bit 2: sparse A
       int it = 0;   // stage counter (also the position in the scale slot ring)
       int local = 0;
       bool ok = true;
@@ -445,22 +459,36 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             break;
           }
           tc_fence_after();
-          int nkb = p.ka - kt * kKBlocksPerStage;
-          if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
-          // Descriptor start addresses are in 16-byte units: +2 per 32-byte K-block.
-          const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 1024, 2);
-          const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
           const int slot = it % C::kSfSlots;
-          const uint32_t sf_t = tmem_base + C::kSfCol + slot * kSfSlotCols;
-          if (nkb == kKBlocksPerStage) {
-#pragma unroll
-            for (int kb = 0; kb < kKBlocksPerStage; ++kb)
-              tc_mma_mxf4nvf4(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
-                              sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
+          if constexpr (SP) {
+            // Two sparse MMAs (128 logical K each): compressed A 32 bytes (+2 descriptor units)
+            // and B 64 bytes (+4) apart; scales one word per row (SFA at +4m, SFB at +8m),
+            // metadata two columns per MMA at +32 in the rows' own lanes.
+            int nm = p.ka - kt * 2;
+            if (nm > 2) nm = 2;
+            const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 512, 4);
+            const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
+            const uint32_t sf_t = tmem_base + C::kSfCol + slot * kSfSlotCols;
+            for (int m = 0; m < nm; ++m)
+              tc_mma_mxf4nvf4_sp(acc_t, ad0 + 2 * m, bd0 + 4 * m, sf_t + 32 + 2 * m, idesc,
+                                 sf_t + 4 * m, sf_t + kSfbOff + 8 * m, (kt > 0 || m > 0) ? 1u : 0u);
           } else {
-            for (int kb = 0; kb < nkb; ++kb)
-              tc_mma_mxf4nvf4(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
-                              sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
+            int nkb = p.ka - kt * kKBlocksPerStage;
+            if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+            // Descriptor start addresses are in 16-byte units: +2 per 32-byte K-block.
+            const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 1024, 2);
+            const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
+            const uint32_t sf_t = tmem_base + C::kSfCol + slot * kSfSlotCols;
+            if (nkb == kKBlocksPerStage) {
+#pragma unroll
+              for (int kb = 0; kb < kKBlocksPerStage; ++kb)
+                tc_mma_mxf4nvf4(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
+                                sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
+            } else {
+              for (int kb = 0; kb < nkb; ++kb)
+                tc_mma_mxf4nvf4(acc_t, ad0 + 2 * kb, bd0 + 2 * kb, idesc, sf_t + kb * 4,
+                                sf_t + kSfbOff + kb * C::kSfbColsPerKb, (kt > 0 || kb > 0) ? 1u : 0u);
+            }
           }
           issued = true;
           tc_commit(smem_u32(&sf_empty[slot]));
@@ -501,7 +529,33 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // MMA rows of quadrant q, so each writer stores that one column per K-block. SFB rows
         // map to accumulator columns, which every quadrant computes: all four words, in every
         // quadrant.
-        uint32_t va[kKBlocksPerStage], vb[4 * C::kSfbColsPerKb];
+        uint32_t va[kKBlocksPerStage], vb[4 * C::kSfbColsPerKb], vm[4];
+        if constexpr (SP) {
+          // Per sparse MMA m (atom kt*2 + m, 128 logical K): SFA word q, SFB all of both row
+          // blocks' words, metadata words 2m, 2m+1 of this row (8 bytes = 16 groups).
+          int nm = p.ka - kt * 2;
+          if (nm > 2) nm = 2;
+          const int row = tm * kBM + q * 32 + lane;
+          const uint8_t* gm = p.meta + static_cast<size_t>(row < p.M ? row : 0) * (p.K / 16) + kt * 16;
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const bool in = m < nm;
+            va[m] = in ? __ldg(reinterpret_cast<const uint32_t*>(ga + q * 4 + (kt * 2 + m) * 512)) : 0u;
+#pragma unroll
+            for (int jb = 0; jb < C::kSfbAtoms; ++jb) {
+              const int rb = tn * (BN / 128) + jb;
+              uint4 x = make_uint4(0u, 0u, 0u, 0u);
+              if (in && rb < p.sfb_rowblocks)
+                x = __ldg(reinterpret_cast<const uint4*>(
+                    p.sfb + (static_cast<size_t>(rb) * p.ka + kt * 2 + m) * 512 + lane * 16));
+              const int o = m * 8 + 4 * jb;
+              vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              vm[2 * m + h] = (in && row < p.M) ? __ldg(reinterpret_cast<const uint32_t*>(gm + 8 * m + 4 * h)) : 0u;
+          }
+        } else {
 #pragma unroll
         for (int kb = 0; kb < kKBlocksPerStage; ++kb) {
           va[kb] = 0u;
@@ -519,6 +573,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
           }
         }
+        }
         // The slot's previous use (stage it - kSfSlots) must have been consumed. This also
         // orders this writer's "full" arrival after that barrier's previous phase, because
         // kSfSlots <= kStages.
@@ -530,10 +585,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         tc_fence_after();
         const uint32_t sf_t = lane_base + C::kSfCol + slot * kSfSlotCols;
+        if constexpr (SP) {
 #pragma unroll
-        for (int kb = 0; kb < kKBlocksPerStage; ++kb) tmem_st_32x32b_x1(sf_t + kb * 4 + q, va[kb]);
-        tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
-        if (C::kSfbAtoms == 2) tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
+          for (int m = 0; m < 2; ++m) tmem_st_32x32b_x1(sf_t + 4 * m + q, va[m]);
+          tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
+          tmem_st_32x32b_x4(sf_t + 32, vm[0], vm[1], vm[2], vm[3]);
+        } else {
+#pragma unroll
+          for (int kb = 0; kb < kKBlocksPerStage; ++kb) tmem_st_32x32b_x1(sf_t + kb * 4 + q, va[kb]);
+          tmem_st_32x32b_x16(sf_t + kSfbOff, vb);
+          if (C::kSfbAtoms == 2) tmem_st_32x32b_x16(sf_t + kSfbOff + 16, vb + 16);
+        }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -586,274 +648,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 }
 
 
-// ---- pair-wise 2:4 sparse kernel (tcgen05.mma.sp): 128 x 128 tiles ---------------------
-// A is stored compressed ([M][K/4] bytes: the 2 kept pairs of every group of 8 K elements)
-// with pair metadata [M][K/16] (a nibble per group: first kept pair | second << 2) and
-// UE4M3 scales per 32 K elements (A and B); B is dense. One sparse MMA covers 128 logical K
-// (32 compressed bytes of A, 64 bytes of B); a stage is 512 logical K, four MMAs: A 16 KB
-// (one 128-byte-wide box) + B 32 KB (two boxes), four stages. The MMA reads, per row and per
-// MMA, one word of A scales and one of B scales (byte j for logical K 32j..32j+31), and two
-// TMEM columns of metadata in the row's own lane (measured on B200 with one-hot probes). The
-// writers load all three from L2 into registers and store them into a ring of two TMEM slots:
-// SFA one column per quadrant (diagonal, as in the dense kernel), SFB whole in every quadrant,
-// metadata 8 columns in the rows' own lanes. Accumulators: two 128-column buffers, no overlap.
-struct SpCfg {
-  static constexpr int kABytes = 128 * 128;                 // 128 rows x 128 B compressed
-  static constexpr int kBBox = 128 * 128;                   // 128 rows x 128 B of B
-  static constexpr int kBBytes = 2 * kBBox;                 // 128 rows x 256 B (512 K)
-  static constexpr int kStageBytes = kABytes + kBBytes;     // 48 KB
-  static constexpr int kStages = 4;
-  static constexpr int kMmas = 4;                           // per stage
-  static constexpr int kCBufBytes = 32 * 32 * 4;
-  static constexpr int kCBytes = 4 * 2 * kCBufBytes;
-  static constexpr int kBarBytes = 512;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
-  static constexpr int kSfSlots = 2;
-  static constexpr int kSlotCols = 48;                      // SFA +0, SFB +16, metadata +32
-  static constexpr int kSfCol = 256;                        // after the two accumulators
-  static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static_assert(kSfCol + kSfSlots * kSlotCols <= kTmemCols, "TMEM budget");
-};
-
-__device__ __forceinline__ void tc_mma_mxf4nvf4_sp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                                   uint32_t meta_tmem, uint32_t idesc, uint32_t sfa_tmem,
-                                                   uint32_t sfb_tmem, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %7, 0;\n\t"
-      "tcgen05.mma.sp.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X "
-      "[%0], %1, %2, [%3], %4, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem),
-      "r"(accumulate)
-      : "memory");
-}
-
-__global__ void __launch_bounds__(kNumThreads, 1)
-    gemm_sparse_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                       const __grid_constant__ CUtensorMap tmap_b,
-                       const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
-  using C = SpCfg;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = sA + C::kStages * C::kABytes;
-  uint8_t* sC = sB + C::kStages * C::kBBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
-  uint64_t* full = bars;                      // A/B bytes + producer + the stage's 4 writers
-  uint64_t* empty = full + C::kStages;
-  uint64_t* sf_empty = empty + C::kStages;
-  uint64_t* acc_full = sf_empty + C::kSfSlots;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_full + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(smem_u32(&full[s]), 1 + 4);
-      mbar_init(smem_u32(&empty[s]), 1);
-    }
-    for (int j = 0; j < C::kSfSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), 4);
-    }
-    mbar_init(smem_u32(drain), 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    prefetch_tmap(&tmap_a);
-    prefetch_tmap(&tmap_b);
-    if (p.tma_store) prefetch_tmap(&tmap_c);
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(p, t, tm, tn);
-        for (int kt = 0; kt < p.num_kt; ++kt, ++it) {
-          const int s = it % C::kStages;
-          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
-          if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word,
-                         kErrWaitSmemEmpty)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = smem_u32(&full[s]);
-          mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes);
-          // Boxes past the end of K read as zeros (and still count their bytes).
-          tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * 128, tm * 128, fb);
-          tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * 256, tn * 128, fb);
-          tma_load_2d(smem_u32(sB + s * C::kBBytes + C::kBBox), &tmap_b, kt * 256 + 128, tn * 128, fb);
-        }
-      }
-      if (!ok) {
-        for (int back = 1; back <= C::kStages && it - back >= 0; ++back) {
-          const int f = it - back;
-          mbar_wait_drain(smem_u32(&full[f % C::kStages]),
-                          static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_mxf4nvf4(kBM, 128) | (1u << 2);  // bit 2: sparse A
-      int it = 0, local = 0;
-      bool ok = true, issued = false;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
-        const int b = local & 1;
-        const uint32_t u = static_cast<uint32_t>(local >> 1);
-        if (!mbar_wait(smem_u32(&acc_empty[b]), (u & 1u) ^ 1u, abort_flag, p.err_word,
-                       kErrWaitAccEmpty)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t acc_t = tmem_base + (b ? 128u : 0u);
-        for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
-          const int s = it % C::kStages;
-          const uint32_t j = static_cast<uint32_t>(it / C::kStages);
-          if (!mbar_spin_wait<false>(smem_u32(&full[s]), j & 1u, abort_flag, p.err_word,
-                                     kErrWaitTmaFull)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int slot = it % C::kSfSlots;
-          int nm = p.ka - kt * C::kMmas;
-          if (nm > C::kMmas) nm = C::kMmas;
-          const uint64_t ad0 = make_sdesc(smem_u32(sA + s * C::kABytes), 16, 1024, 2);
-          const uint64_t bd0 = make_sdesc(smem_u32(sB + s * C::kBBytes), 16, 1024, 2);
-          const uint64_t bd1 = make_sdesc(smem_u32(sB + s * C::kBBytes + C::kBBox), 16, 1024, 2);
-          const uint32_t sf_t = tmem_base + C::kSfCol + slot * C::kSlotCols;
-          // MMA m: compressed A bytes 32m.. (+2 descriptor units each), B box m/2 at byte
-          // 64 (m % 2) (+4 units).
-          for (int m = 0; m < nm; ++m)
-            tc_mma_mxf4nvf4_sp(acc_t, ad0 + 2 * m, ((m >> 1) ? bd1 : bd0) + 4 * (m & 1),
-                               sf_t + 32 + 2 * m, idesc, sf_t + 4 * m, sf_t + 16 + 4 * m,
-                               (kt > 0 || m > 0) ? 1u : 0u);
-          issued = true;
-          tc_commit(smem_u32(&sf_empty[slot]));
-          tc_commit(smem_u32(&empty[s]));
-        }
-        if (!ok) break;
-        tc_commit(smem_u32(&acc_full[b]));
-      }
-      if (!ok && issued) {
-        tc_commit(smem_u32(drain));
-        mbar_wait_drain(smem_u32(drain), 0, p.err_word);
-      }
-    }
-  } else if (warp >= 6) {
-    // ------------------------------------------------------------------ scale + metadata writers
-    const int q = warp & 3;
-    const int wgroup = (warp - 6) >> 2;
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    const int mrow_bytes = p.K / 16;
-    int it = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(p, t, tm, tn);
-      const int row = tm * 128 + q * 32 + lane;
-      const uint8_t* ga = p.sfa + static_cast<size_t>(tm) * p.ka * 512 + lane * 16 + q * 4;
-      const uint8_t* gb = p.sfb + static_cast<size_t>(tn) * p.ka * 512 + lane * 16;
-      const uint8_t* gm = p.meta + static_cast<size_t>(row < p.M ? row : 0) * mrow_bytes;
-      for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
-        if ((it % kWriterGroups) != wgroup) continue;
-        const int s = it % C::kStages;
-        const int slot = it % C::kSfSlots;
-        int nm = p.ka - kt * C::kMmas;
-        if (nm > C::kMmas) nm = C::kMmas;
-        uint32_t va[C::kMmas], vb[16], vm[8];
-#pragma unroll
-        for (int m = 0; m < C::kMmas; ++m) {
-          const bool in = m < nm;
-          va[m] = in && tm < p.sfa_rowblocks
-                      ? __ldg(reinterpret_cast<const uint32_t*>(ga + (kt * C::kMmas + m) * 512)) : 0u;
-          uint4 x = make_uint4(0u, 0u, 0u, 0u);
-          if (in && tn < p.sfb_rowblocks)
-            x = __ldg(reinterpret_cast<const uint4*>(gb + (kt * C::kMmas + m) * 512));
-          vb[4 * m] = x.x; vb[4 * m + 1] = x.y; vb[4 * m + 2] = x.z; vb[4 * m + 3] = x.w;
-          // Metadata words 2m, 2m+1: groups 16m..16m+15 of this stage (4 bytes each).
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int off = kt * 32 + 8 * m + 4 * h;
-            vm[2 * m + h] = (in && row < p.M && off < mrow_bytes)
-                                ? __ldg(reinterpret_cast<const uint32_t*>(gm + off)) : 0u;
-          }
-        }
-        // The slot's previous use must have been consumed (and, slots <= stages, the stage's
-        // "full" barrier has finished its previous phase).
-        if (!mbar_wait(smem_u32(&sf_empty[slot]),
-                       (static_cast<uint32_t>(it / C::kSfSlots) & 1u) ^ 1u, abort_flag,
-                       p.err_word, kErrWaitSfEmpty)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sf_t = lane_base + C::kSfCol + slot * C::kSlotCols;
-#pragma unroll
-        for (int m = 0; m < C::kMmas; ++m) tmem_st_32x32b_x1(sf_t + 4 * m + q, va[m]);
-        tmem_st_32x32b_x16(sf_t + 16, vb);
-        tmem_st_32x32b_x8(sf_t + 32, vm);
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&full[s]));
-      }
-    }
-  } else {
-    // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int row_in_tile = q * 32 + lane;
-    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0};
-    int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
-      const int b = local & 1;
-      const uint32_t u = static_cast<uint32_t>(local >> 1);
-      if (!mbar_wait(smem_u32(&acc_full[b]), u & 1u, abort_flag, p.err_word, kErrWaitAccFull))
-        break;
-      tc_fence_after();
-      int tm, tn;
-      tile_coords(p, t, tm, tn);
-      const int row = tm * kBM + row_in_tile;
-      const int col_base = tn * 128;
-      e.row0 = tm * kBM + q * 32;
-      const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (b ? 128u : 0u);
-#pragma unroll
-      for (int c = 0; c < 4; c += 2) {
-        const int g[2] = {c, c + 1};
-        epi_group<2>(p, e, acc_t, g, row, col_base, 0);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
-    }
-    if (lane == 0) bulk_wait_group<0>();
-    __syncwarp();
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
-}
+// ---- pair-wise 2:4 sparse variant (gemm_mxf4nvf4_kernel<256, true>) --------------------
+// A is stored compressed ([M][K/4] bytes: the 2 kept pairs of every group of 8 K elements) with
+// pair metadata [M][K/16] (a nibble per group: first kept pair | second << 2) and UE4M3 scales
+// per 32 K elements (A and B); B is dense. One sparse MMA covers 128 logical K (32 compressed
+// bytes of A, 64 bytes of B); a stage is 256 logical K: A 8 KB (one 64-byte-wide, 64-byte-
+// swizzled box) + B 32 KB, two MMAs of 128 x 256, four stages - the dense 128 x 256 kernel's
+// structure, tile order, epilogue and accumulator overlap. Per row and per MMA the MMA reads
+// one word of A scales and one of B scales (byte j for logical K 32j..32j+31) and two TMEM
+// columns of metadata in the row's own lane (measured on B200 with one-hot probes); the writers
+// load them from L2 and store SFA diagonally, SFB whole and the metadata at slot column +32.
 
 // ---- SM-pair kernel (cta_group::2): 256 x 256 tiles ------------------------------------
 // The two CTAs of a cluster work on one 256 x 256 output tile. Each loads its own 128 rows
@@ -1179,8 +983,10 @@ EncodeTiledFn get_encode_fn() {
 
 // Packed FP4 rows as a 2-D UINT8 tensor [rows][K/2], box {128 bytes, box_rows}, 128-byte
 // swizzle, zero fill out of bounds.
+// Packed operand [rows][K/2] bytes, K-major. sw64: a 64-byte-wide box with 64-byte swizzle (the
+// sparse kernel's compressed A stage); otherwise 128 bytes with 128-byte swizzle.
 bool encode_operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows,
-                        std::string* err) {
+                        std::string* err, bool sw64 = false) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) {
     set_err(err, "cuTensorMapEncodeTiled unavailable from the driver");
@@ -1188,10 +994,11 @@ bool encode_operand_map(CUtensorMap* map, const void* base, int rows, int K, int
   }
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBKBytes), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(sw64 ? 64 : kBKBytes), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   sw64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_err(err, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
@@ -1230,7 +1037,7 @@ bool encode_output_map(CUtensorMap* map, void* base, int M, int N, bool bf16, st
 struct MapKey {
   const void* base;
   long rows, cols;
-  int box, kind;  // kind: 0 = operand, 1 = BF16 output, 2 = FP32 output
+  int box, kind;  // kind: 0 = operand, 1 = BF16 output, 2 = FP32 output, 3 = operand, 64-byte box
   bool operator==(const MapKey& o) const {
     return base == o.base && rows == o.rows && cols == o.cols && box == o.box && kind == o.kind;
   }
@@ -1254,8 +1061,9 @@ bool cached_map(const MapKey& k, CUtensorMap* out, std::string* err) {
         return true;
       }
   }
-  bool ok = k.kind == 0 ? encode_operand_map(out, k.base, static_cast<int>(k.rows),
-                                             static_cast<int>(k.cols), k.box, err)
+  bool ok = (k.kind == 0 || k.kind == 3)
+                ? encode_operand_map(out, k.base, static_cast<int>(k.rows), static_cast<int>(k.cols),
+                                     k.box, err, k.kind == 3)
                         : encode_output_map(out, const_cast<void*>(k.base), static_cast<int>(k.rows),
                                             static_cast<int>(k.cols), k.kind == 1, err);
   if (!ok) return false;
@@ -1272,9 +1080,8 @@ struct DeviceState {
   bool init = false;
   int sms = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[2] = {false, false};
+  bool attr_set[3] = {false, false, false};
   bool pair_attr_set = false;
-  bool sparse_attr_set = false;
   int pair_clusters = 0;  // co-resident SM-pair clusters of the pair kernel
   uint32_t* err_word = nullptr;
   // Workspace for canonical -> tcgen05 scale reordering (grown on demand).
@@ -1314,14 +1121,14 @@ DeviceState* device_state(std::string* err) {
   return &d;
 }
 
-template <int BN>
+template <int BN, bool SP = false>
 bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                   const GemmParams& p,
                   DeviceState* ds, cudaStream_t s, std::string* err) {
-  using C = Cfg<BN>;
-  const int idx = BN == 256 ? 1 : 0;
+  using C = Cfg<BN, SP>;
+  const int idx = SP ? 2 : (BN == 256 ? 1 : 0);
   if (!ds->attr_set[idx]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_mxf4nvf4_kernel<BN>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_mxf4nvf4_kernel<BN, SP>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess) {
@@ -1331,7 +1138,7 @@ bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     ds->attr_set[idx] = true;
   }
   int grid = p.num_tiles < ds->sms ? p.num_tiles : ds->sms;
-  gemm_mxf4nvf4_kernel<BN><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, tc, p);
+  gemm_mxf4nvf4_kernel<BN, SP><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, tc, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_err(err, std::string("gemm launch: ") + cudaGetErrorString(e));
@@ -1570,8 +1377,8 @@ bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err
     set_err(err, "sparse mode needs positive M, N and K a multiple of 128");
     return false;
   }
-  if (op.cta_group == 2 || (op.tile_n != 0 && op.tile_n != 128)) {
-    set_err(err, "sparse mode runs 128 x 128 one-SM tiles (cta_group 0/1, tile_n 0/128)");
+  if (op.cta_group == 2 || (op.tile_n != 0 && op.tile_n != 256)) {
+    set_err(err, "sparse mode runs 128 x 256 one-SM tiles (cta_group 0/1, tile_n 0/256)");
     return false;
   }
   if ((reinterpret_cast<uintptr_t>(op.a_packed) | reinterpret_cast<uintptr_t>(op.b_packed)) & 15 ||
@@ -1619,42 +1426,26 @@ bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err
   p.alpha = op.a_global * op.b_global;
   p.out_bf16 = (op.d != nullptr && op.out_dtype == OutDType::BF16) ? 1 : 0;
   p.tiles_m = (op.M + 127) / 128;
-  p.tiles_n = (op.N + 127) / 128;
+  p.tiles_n = (op.N + 255) / 256;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.group_m = 16;
   p.ka = (op.K + 127) / 128;          // MMAs (and scale atoms) along K
-  p.num_kt = (op.K + 511) / 512;
+  p.num_kt = (op.K + 255) / 256;      // 256-K stages
   p.sfb_rowblocks = (op.N + 127) / 128;
   p.sfa_rowblocks = (op.M + 127) / 128;
   p.err_word = ds->err_word;
   if (!setup_nvfp4_out(op, p, s, err)) return false;
   CUtensorMap ta, tb, tc;
-  // Compressed A: [M][K/4] bytes, i.e. a packed operand of K/2 columns.
-  if (!cached_map(MapKey{op.a_packed, op.M, vk, 128, 0}, &ta, err)) return false;
-  if (!cached_map(MapKey{op.b_packed, op.N, op.K, 128, 0}, &tb, err)) return false;
+  // Compressed A: [M][K/4] bytes, i.e. a packed operand of K/2 columns, in 64-byte boxes.
+  if (!cached_map(MapKey{op.a_packed, op.M, vk, 128, 3}, &ta, err)) return false;
+  if (!cached_map(MapKey{op.b_packed, op.N, op.K, 256, 0}, &tb, err)) return false;
   std::memset(&tc, 0, sizeof(tc));
   const int esize = p.out_bf16 ? 2 : 4;
   p.tma_store = (!p.out_nvfp4 && (static_cast<size_t>(op.N) * esize) % 16 == 0 &&
                  (reinterpret_cast<uintptr_t>(out) & 15) == 0) ? 1 : 0;
   if (p.tma_store && !cached_map(MapKey{out, op.M, op.N, 32, p.out_bf16 ? 1 : 2}, &tc, err))
     return false;
-  if (!ds->sparse_attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_sparse_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SpCfg::kSmemBytes);
-    if (e != cudaSuccess) {
-      set_err(err, std::string("cudaFuncSetAttribute (sparse): ") + cudaGetErrorString(e));
-      return false;
-    }
-    ds->sparse_attr_set = true;
-  }
-  const int grid = p.num_tiles < ds->sms ? p.num_tiles : ds->sms;
-  gemm_sparse_kernel<<<grid, kNumThreads, SpCfg::kSmemBytes, s>>>(ta, tb, tc, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_err(err, std::string("sparse launch: ") + cudaGetErrorString(e));
-    return false;
-  }
-  return true;
+  return launch_dense<256, true>(ta, tb, tc, p, ds, s, err);
 }
 
 bool operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows,
