@@ -3,17 +3,24 @@
 4096x14336x4096 and % of the measured tcgen05 FP4 peak).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--config c2|c1|c3|decode-up-16|...]
+                    [--config c2|c1|c3|c3-16k|c4|decode-{up,down}-{16,64,128}]
+                    [--gather] [--quantize-a] [--kernel-only] [--no-cpu-baseline]
 
 One step = one D = A*B^T launch of the workload (config 2 of BASELINE.json by default:
 M=4096 tokens, N=14336, K=4096, N(0,1) operands quantised on the GPU to E2M1/UE4M3, BF16 out).
-Under torchrun every rank computes its own N-slice of a problem N*world wide (weak scaling,
-no data-path collective). Rank 0 prints one JSON line.
+c4 is the pair-wise 2:4 sparse configuration (the format the tcgen05 .sp MMA executes);
+decode-* are the M <= 128 weight-streaming shapes. Under torchrun every rank computes its own
+N-slice of a problem N*world wide (weak scaling, no data-path collective), except c3-16k,
+whose N = 65536 is split over the ranks (strong scaling); --gather also times the optional
+NCCL all-gather of the C shards. Rank 0 prints one JSON line.
 
-`value` is device-timed: operands resident in HBM, L2 flushed (256 MiB write) before every
-step, CUDA events around each launch on the launching stream, max over ranks. `e2e` is the
-same metric through the C ABI with pinned host buffers: each step copies the quantised
-operands host->device, launches, and copies C device->host, all inside the timed region.
+`value` is device-timed with operands resident in HBM: for M > 128 the L2 is flushed (256 MiB
+write) before every step and CUDA events bracket each launch; decode shapes rotate the weight
+over copies larger than 3x L2 and time the K back-to-back steps with one event pair (the next
+launch's prologue overlaps through programmatic dependent launch); max over ranks.
+--quantize-a adds the GPU quantisation of fp32 A to every (decode) step. `e2e` is the same
+metric through the C ABI with pinned host buffers: each step copies the quantised operands
+host->device, launches, and copies C device->host, all inside the timed region.
 `--impl reference` times the reference's own algorithm for this path on the host cores (the
 CPU restatement of src/reference.cu in oracle/, over dequantised operands) on a bounded
 sample of output rows; it never touches the GPU.

@@ -30,8 +30,9 @@
 //               SFA rows map to TMEM lanes, and the MMA rows of quadrant q read only column q
 //               of each 4-column SFA group, so each writer stores just that column (a quarter
 //               of the bytes; verified bit-exact by the integer known-answer test).
-//               TMEM stores from other warps slow the MMAs that share the TMEM (measured: 16%
-//               faster with no scale stores at all), so fewer bytes is faster. tcgen05.cp
+//               The kernel ran 16% faster with no scale stores at all (an isolated MMA stream
+//               is not slowed by concurrent TMEM stores; the interaction inside the kernel is
+//               not isolated yet), and fewer bytes measured faster. tcgen05.cp
 //               would do the copy on the tensor pipe, in series with the MMAs (4 MMAs of a
 //               stage take 512 cycles, 980 with the stage's 12 copies). Scales take no shared
 //               memory, which leaves room for a fourth A/B stage: more bytes in flight for the
@@ -41,6 +42,9 @@
 // columns side by side, so buffer 1 starts at column 160: the epilogue loads the 3 chunks
 // that hold the 96 shared columns first, releases them ("acc_early") as soon as they are in
 // registers, and drains the rest afterwards.
+//
+// The same kernel with SP = true is the pair-wise 2:4 sparse GEMM (tcgen05.mma.sp; see its
+// section below), and any of the kernels can write C as NVFP4 (store_chunk_nvfp4).
 //
 // Every mbarrier wait is bounded (ptx.cuh); a timeout sets the device error word, all roles
 // leave their loops, in-flight copies and MMAs are drained with bounded waits, TMEM is freed
