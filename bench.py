@@ -241,9 +241,12 @@ def run_b200(args, rank, world, local_rank):
     del x
     C = torch.empty((M, N), dtype=out_dtype, device=dev)
     mode = api.MODE_SPARSE24 if sparse else api.MODE_DENSE
+    # --quantize-a: the weights are never written by the quantisation that precedes each
+    # GEMM, so the decode kernel may start streaming them before it completes (b_static).
     gargs = api.gemm_args(A.packed, A.scales_tc, B.packed, B.scales_tc, M, N, K, C,
                           sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
-                          cta_group=args.cta_group, mode=mode, a_meta=a_meta)
+                          cta_group=args.cta_group, mode=mode, a_meta=a_meta,
+                          b_static=args.quantize_a)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
@@ -280,7 +283,7 @@ def run_b200(args, rank, world, local_rank):
             keep.append((bp, bs))
             rot.append(api.gemm_args(A.packed, A.scales_tc, bp, bs, M, N, K, C,
                                      sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
-                                     cta_group=args.cta_group))
+                                     cta_group=args.cta_group, b_static=args.quantize_a))
     step_no = [0]
     # --quantize-a (decode): every step first quantises the fp32 activations A into the tcgen05
     # layout the GEMM reads (the per-call cost of a real decode layer), then runs the GEMM.

@@ -54,6 +54,10 @@ struct Nvfp4DeviceOperands {
   uint8_t* d_scales = nullptr;
   float d_global = 1.0f;
   SfLayout d_sf_layout = SfLayout::Canonical;
+  // The caller guarantees that B and its scales are not written by the work enqueued just
+  // before this call on the stream: the decode kernel may then start streaming the weight
+  // before that work completes (programmatic dependent launch).
+  bool b_static = false;
 };
 
 // src/gemm.h:25-29. Each backend returns true on success; on failure it sets *err (which

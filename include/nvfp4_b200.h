@@ -54,7 +54,13 @@ typedef struct Nvfp4GemmArgs {
   void* c_scales;
   float c_global;
   int c_sf_layout;
+  int flags;            /* NVFP4_FLAG_* */
 } Nvfp4GemmArgs;
+
+/* Nvfp4GemmArgs.flags. B_STATIC: B and its scales are not written by the work enqueued just
+ * before this call on the stream, so the decode kernel may start streaming the weight before
+ * that work completes (e.g. while this layer's activations are being quantised). */
+enum { NVFP4_FLAG_B_STATIC = 1 };
 
 /* Replaces launch_gemm(KernelKind::Custom, op, s, err) - src/gemm.h:31-40 and the
  * custom backend src/gemm_custom.cu:134-159 - with the tcgen05 backend. With

@@ -22,6 +22,7 @@ LIB_PATH = os.environ.get("NVFP4_B200_LIB", _build.LIB)
 MODE_DENSE, MODE_SPARSE24 = 0, 1
 SF_CANONICAL, SF_TCGEN05 = 0, 1
 OUT_F32, OUT_BF16, OUT_NVFP4 = 0, 1, 2
+FLAG_B_STATIC = 1
 
 # Every symbol include/nvfp4_b200.h declares (checked by the CPU tests).
 EXPORTED = [
@@ -53,6 +54,7 @@ class GemmArgs(C.Structure):
         ("mode", C.c_int), ("sf_layout", C.c_int), ("out_dtype", C.c_int),
         ("a_meta", C.c_void_p), ("cta_group", C.c_int), ("tile_n", C.c_int),
         ("c_scales", C.c_void_p), ("c_global", C.c_float), ("c_sf_layout", C.c_int),
+        ("flags", C.c_int),
     ]
 
 
@@ -156,7 +158,8 @@ def gemm_args(a_packed, a_scales, b_packed, b_scales, M, N, K, out, **kw) -> Gem
                     kw.get("mode", MODE_DENSE), kw.get("sf_layout", SF_TCGEN05), od,
                     _ptr(kw.get("a_meta")), kw.get("cta_group", 0), kw.get("tile_n", 0),
                     _ptr(kw.get("out_scales")), kw.get("out_global", 1.0),
-                    kw.get("out_sf_layout", SF_CANONICAL))
+                    kw.get("out_sf_layout", SF_CANONICAL),
+                    FLAG_B_STATIC if kw.get("b_static") else 0)
 
 
 def launch(args: GemmArgs, stream=None) -> None:

@@ -91,6 +91,7 @@ int nvfp4_b200_gemm(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errl
   op.a_meta = static_cast<const uint8_t*>(a->a_meta);
   op.cta_group = a->cta_group;
   op.tile_n = a->tile_n;
+  op.b_static = (a->flags & NVFP4_FLAG_B_STATIC) != 0;
   std::string e;
   if (!launch_gemm_b200(op, static_cast<cudaStream_t>(stream), &e))
     return fail(classify(e), e, err, errlen);

@@ -53,6 +53,7 @@ struct DParams {
   float alpha;
   int out_bf16;
   int tiles_n, splits, num_kt, ka;
+  int b_static;         // the weight may be read before the preceding kernel completes
   uint32_t* err_word;
 };
 
@@ -153,8 +154,11 @@ __global__ void __launch_bounds__(kDThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Launched with programmatic stream serialization: the set-up above overlaps the previous
-  // kernel on the stream; every global read and write comes after it has completed.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // kernel on the stream. Every thread that reads or writes global memory first waits for
+  // that kernel to complete (griddepcontrol.wait) - except that with b_static the producer
+  // starts loading the first stages' weight bytes before its wait (the caller guarantees the
+  // weight is not written by the preceding work), so the weight stream overlaps e.g. the
+  // quantisation of this layer's activations.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
@@ -162,7 +166,43 @@ __global__ void __launch_bounds__(kDThreads, 1)
     if (lane == 0) {
       bool ok = true;
       int i = 0;
-      for (int kt = kt0; kt < kt1; ++kt, ++i) {
+      // Weight half of a stage (tiles + scale atoms) and token half; both count their bytes
+      // on the stage's barriers, which expect the whole stage up front.
+      auto issue_w = [&](int kt, int s) {
+        int nkb = p.ka - kt * C::kKb;
+        if (nkb > C::kKb) nkb = C::kKb;
+        const uint32_t sfb = static_cast<uint32_t>(nkb) * 512u;
+        const uint32_t db = smem_u32(&sfd[s]), fb = smem_u32(&full[s]);
+        mbar_arrive_expect_tx(db, 2 * sfb);
+        mbar_arrive_expect_tx(fb, C::kWBytes + C::kTBytes);
+        bulk_load(smem_u32(sSFW + s * C::kSfBytes),
+                  p.sfw + (static_cast<size_t>(tn) * p.ka + kt * C::kKb) * 512, sfb, db);
+        // Boxes past the end of K read as zeros (and still count their bytes).
+#pragma unroll
+        for (int h = 0; h < C::kHalves; ++h)
+          tma_load_2d(smem_u32(sW + s * C::kWBytes + h * 128 * 128), &tmap_w,
+                      kt * C::kKb * 32 + h * 128, tn * 128, fb);
+      };
+      auto issue_t = [&](int kt, int s) {
+        int nkb = p.ka - kt * C::kKb;
+        if (nkb > C::kKb) nkb = C::kKb;
+        bulk_load(smem_u32(sSFT + s * C::kSfBytes), p.sft + static_cast<size_t>(kt) * C::kKb * 512,
+                  static_cast<uint32_t>(nkb) * 512u, smem_u32(&sfd[s]));
+#pragma unroll
+        for (int h = 0; h < C::kHalves; ++h)
+          tma_load_2d(smem_u32(sT + s * C::kTBytes + h * MPAD * 128), &tmap_t,
+                      kt * C::kKb * 32 + h * 128, 0, smem_u32(&full[s]));
+      };
+      // The first pass through the ring needs no "empty" wait.
+      int pre = 0;
+      if (p.b_static) {
+        pre = kt1 - kt0 < C::kStages ? kt1 - kt0 : C::kStages;
+        for (int q2 = 0; q2 < pre; ++q2) issue_w(kt0 + q2, q2);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int q2 = 0; q2 < pre; ++q2) issue_t(kt0 + q2, q2);
+      i = pre;
+      for (int kt = kt0 + pre; kt < kt1; ++kt, ++i) {
         const int s = i % C::kStages;
         const uint32_t j = static_cast<uint32_t>(i / C::kStages);
         if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word,
@@ -170,24 +210,8 @@ __global__ void __launch_bounds__(kDThreads, 1)
           ok = false;
           break;
         }
-        int nkb = p.ka - kt * C::kKb;
-        if (nkb > C::kKb) nkb = C::kKb;
-        const uint32_t sfb = static_cast<uint32_t>(nkb) * 512u;
-        const uint32_t db = smem_u32(&sfd[s]);
-        mbar_arrive_expect_tx(db, 2 * sfb);
-        bulk_load(smem_u32(sSFW + s * C::kSfBytes),
-                  p.sfw + (static_cast<size_t>(tn) * p.ka + kt * C::kKb) * 512, sfb, db);
-        bulk_load(smem_u32(sSFT + s * C::kSfBytes),
-                  p.sft + static_cast<size_t>(kt) * C::kKb * 512, sfb, db);
-        const uint32_t fb = smem_u32(&full[s]);
-        mbar_arrive_expect_tx(fb, C::kWBytes + C::kTBytes);
-        // Boxes past the end of K read as zeros (and still count their bytes).
-#pragma unroll
-        for (int h = 0; h < C::kHalves; ++h) {
-          const int x = kt * C::kKb * 32 + h * 128;
-          tma_load_2d(smem_u32(sW + s * C::kWBytes + h * 128 * 128), &tmap_w, x, tn * 128, fb);
-          tma_load_2d(smem_u32(sT + s * C::kTBytes + h * MPAD * 128), &tmap_t, x, 0, fb);
-        }
+        issue_w(kt, s);
+        issue_t(kt, s);
       }
       if (!ok) {
         // The most recent fill of every stage lands before the CTA exits ("full" also counts
@@ -289,6 +313,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
     const int n_local = q * 32 + lane;
     const int n = tn * 128 + n_local;
     const bool ok = mbar_wait(smem_u32(acc_full), 0, abort_flag, p.err_word, kErrWaitAccFull);
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // before any store of C
     tc_fence_after();
     const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll
@@ -317,6 +342,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, kDTmemCols);
 
   if (p.splits > 1) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // before any store of C
     // Every CTA of the cluster has its partials in shared memory after this barrier.
     cluster_sync();
     // CTA ks reduces tokens [m0, m1) over the cluster, in rank order.
@@ -442,6 +468,7 @@ bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_
   p.num_kt = 0;  // K-stages: set per stage depth in launch_decode
   p.ka = (op.K + 63) / 64;
   p.splits = 1;
+  p.b_static = op.b_static ? 1 : 0;
   p.err_word = device_error_word(err);
   if (!p.err_word) return false;
   DecodeState* st = nullptr;

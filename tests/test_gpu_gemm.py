@@ -172,3 +172,23 @@ def test_fresh_operand_buffers_reproduce(api, cta_group):
                        tile_n=256)
         assert torch.equal(got, ref)
         del a2, b2
+
+
+@pytest.mark.parametrize("shape", [(16, 4096, 14336), (64, 14336, 4096), (100, 2000, 1024)])
+def test_decode_b_static_is_identical(api, shape):
+    """b_static only lets the decode kernel read the weight before the preceding kernel ends;
+    the result must not change (here the preceding kernel quantises A on the same stream)."""
+    M, N, K = shape
+    x, a = make_operand(api, M, K, 71)
+    _, b = make_operand(api, N, K, 72)
+    ref = run_gemm(api, a, b, M, N, K)
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    g = api.gemm_args(a.packed, a.scales_tc, b.packed, b.scales_tc, M, N, K, out, b_static=True)
+    for _ in range(3):
+        api.quantize(x, a.global_scale)          # re-quantise A just before the GEMM
+        a2 = api.quantize(x, a.global_scale)
+        g = api.gemm_args(a2.packed, a2.scales_tc, b.packed, b.scales_tc, M, N, K, out, b_static=True)
+        api.launch(g)
+        torch.cuda.synchronize()
+        assert api.device_error() == 0
+        assert torch.equal(out, ref)
