@@ -11,9 +11,9 @@
 //               FP4, both 128-byte-swizzled K-major) completing on one mbarrier ("full").
 //               Four 48 KB stages (BN = 256) or six 32 KB stages (BN = 128). No multicast.
 //   warp 1      MMA issuer (one lane): per K-stage, four tcgen05.mma kind::mxf4nvf4
-//               block_scale (M=128, N=BN, K=64) back to back. tcgen05.commit frees the scale
-//               slot ("sf_empty") and the smem stage ("empty") and, per tile, publishes the
-//               accumulator ("acc_full").
+//               block_scale (M=128, N=BN, K=64) back to back. One tcgen05.commit per stage
+//               frees the smem stage and its TMEM scale slot ("empty") and, per tile,
+//               publishes the accumulator ("acc_full").
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, scale by alpha, convert to
 //               FP32/BF16, write the 32 x 32 chunk into a swizzled, double-buffered shared
 //               tile and store it with one TMA tensor store (clipped at the matrix edges).
@@ -94,8 +94,8 @@ struct Cfg {
   static constexpr int kCBytes = 4 * 2 * kCBufBytes;            // 4 warps, double-buffered
   static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
-  // TMEM: a ring of scale slots at the top (freed by "sf_empty", independent of the smem
-  // stages), two accumulator buffers below; which 32-column chunks the buffers share.
+  // TMEM: a ring of scale slots at the top (slot it % kSfSlots, freed with the smem stage
+  // that used it last), two accumulator buffers below; which 32-column chunks the buffers share.
   static constexpr int kSfSlots = NVFP4_SF_SLOTS;
   static_assert(kSfSlots <= kStages, "a writer's slot wait must also order its full[] arrival");
   static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;  // 368
@@ -355,8 +355,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
   uint64_t* full = bars;                // A/B bytes + producer + the stage's 4 scale writers
   uint64_t* empty = bars + C::kStages;  // smem stage consumed
-  uint64_t* sf_empty = empty + C::kStages;  // TMEM scale slot consumed
-  uint64_t* acc_full = sf_empty + C::kSfSlots;
+  uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* acc_early = acc_full + 4;
   uint64_t* drain = acc_full + 6;
@@ -371,7 +370,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&full[s]), 1 + 4);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    for (int j = 0; j < C::kSfSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&acc_empty[b]), 4);
@@ -495,7 +493,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
           }
           issued = true;
-          tc_commit(smem_u32(&sf_empty[slot]));
+          // One commit frees both the smem stage and its TMEM scale slot: the writers of a
+          // slot wait on "empty" of the stage that used it last (a second commit per stage
+          // costs about 60 cycles of MMA issue).
           tc_commit(smem_u32(&empty[s]));
         }
         if (!ok) break;
@@ -578,14 +578,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
         }
-        // The slot's previous use (stage it - kSfSlots) must have been consumed. This also
-        // orders this writer's "full" arrival after that barrier's previous phase, because
-        // kSfSlots <= kStages.
-        if (!mbar_wait(smem_u32(&sf_empty[slot]),
-                       (static_cast<uint32_t>(it / C::kSfSlots) & 1u) ^ 1u, abort_flag,
-                       p.err_word, kErrWaitSfEmpty)) {
-          ok = false;
-          break;
+        // The slot's previous use (stage u = it - kSfSlots) must have been consumed: wait for
+        // phase u / kStages of that stage's "empty". That barrier cannot be a phase further on,
+        // since its next phase needs the MMAs of stage u + kStages > it, which wait for this
+        // writer. This also orders the "full" arrival below after that barrier's previous
+        // phase, because kSfSlots <= kStages.
+        if (it >= C::kSfSlots) {
+          const int u = it - C::kSfSlots;
+          if (!mbar_wait(smem_u32(&empty[u % C::kStages]),
+                         static_cast<uint32_t>(u / C::kStages) & 1u, abort_flag, p.err_word,
+                         kErrWaitSfEmpty)) {
+            ok = false;
+            break;
+          }
         }
         tc_fence_after();
         const uint32_t sf_t = lane_base + C::kSfCol + slot * kSfSlotCols;
@@ -672,7 +677,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 // TMEM. Barriers that gather both CTAs live in the leader: "full" (both CTAs' A/B byte
 // counts through TMA with .cta_group::2 plus both CTAs' scale writers, 1 + 8 arrivals) and the
 // accumulator releases ("acc_empty", "acc_early", 8 arrivals); the leader's commits signal
-// each CTA's own "empty", "sf_empty" and "acc_full" by address.
+// each CTA's own "empty" (stage and scale slot) and "acc_full" by address.
 struct PairCfg {
   static constexpr int kABytes = 128 * kBKBytes;       // this CTA's 128 rows of A
   static constexpr int kBBytes = 128 * kBKBytes;       // this CTA's 128 rows of B
@@ -707,8 +712,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;       // leader, 8 arrivals
   uint64_t* acc_early = acc_full + 4;       // leader, 8 arrivals
-  uint64_t* sf_empty = acc_full + 6;        // each CTA: scale slot consumed
-  uint64_t* drain = sf_empty + C::kSfSlots;
+  uint64_t* drain = acc_full + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -729,7 +733,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&acc_empty[b]), 8);
       mbar_init(smem_u32(&acc_early[b]), 8);
     }
-    for (int j = 0; j < C::kSfSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -835,8 +838,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                    sf_t + kSfbOff + kb * 8, (kt > 0 || kb > 0) ? 1u : 0u);
           }
           issued = true;
-          tc_commit_pair(smem_u32(&sf_empty[slot]));
-          tc_commit_pair(to_peer(&sf_empty[slot]));
+          // "empty" also frees the stage's TMEM scale slot in both CTAs.
           tc_commit_pair(smem_u32(&empty[s]));
           tc_commit_pair(to_peer(&empty[s]));
         }
@@ -889,14 +891,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
           }
         }
-        // The slot's previous use (stage it - kSfSlots) must have been consumed; because
-        // kSfSlots <= kStages this also orders the arrival below after the leader's "full"
-        // barrier finished its previous phase.
-        if (!mbar_wait_cluster(smem_u32(&sf_empty[slot]),
-                               (static_cast<uint32_t>(it / C::kSfSlots) & 1u) ^ 1u, abort_flag,
-                               p.err_word, kErrWaitSfEmpty)) {
-          ok = false;
-          break;
+        // The slot's previous use (stage u = it - kSfSlots) must have been consumed: phase
+        // u / kStages of this CTA's "empty" for that stage (it cannot be a phase further on,
+        // whose MMAs wait for this writer). Because kSfSlots <= kStages this also orders the
+        // arrival below after the leader's "full" barrier finished its previous phase.
+        if (it >= C::kSfSlots) {
+          const int u = it - C::kSfSlots;
+          if (!mbar_wait_cluster(smem_u32(&empty[u % C::kStages]),
+                                 static_cast<uint32_t>(u / C::kStages) & 1u, abort_flag,
+                                 p.err_word, kErrWaitSfEmpty)) {
+            ok = false;
+            break;
+          }
         }
         tc_fence_after();
         const uint32_t sf_t = lane_base + C::kSfCol + slot * kSfSlotCols;

@@ -120,8 +120,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
   uint64_t* full = bars;                      // operand bytes + producer + 4 scale writers
   uint64_t* empty = full + C::kStages;        // smem stage consumed
   uint64_t* sfd = empty + C::kStages;         // the stage's scale atoms landed
-  uint64_t* sf_empty = sfd + C::kStages;      // TMEM scale slot consumed
-  uint64_t* acc_full = sf_empty + C::kSlots;
+  uint64_t* acc_full = sfd + C::kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -138,7 +137,6 @@ __global__ void __launch_bounds__(kDThreads, 1)
       mbar_init(smem_u32(&empty[s]), 1);
       mbar_init(smem_u32(&sfd[s]), 1);
     }
-    for (int j = 0; j < C::kSlots; ++j) mbar_init(smem_u32(&sf_empty[j]), 1);
     mbar_init(smem_u32(acc_full), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -260,8 +258,7 @@ __global__ void __launch_bounds__(kDThreads, 1)
           for (int kb = 0; kb < nkb; ++kb) mma(kb);
         }
         issued = true;
-        tc_commit(smem_u32(&sf_empty[slot]));
-        tc_commit(smem_u32(&empty[s]));
+        tc_commit(smem_u32(&empty[s]));  // also frees the stage's TMEM scale slot
       }
       // acc_full also tells the epilogue that every MMA has finished reading shared memory.
       if (ok || issued) tc_commit(smem_u32(acc_full));
@@ -291,10 +288,14 @@ __global__ void __launch_bounds__(kDThreads, 1)
         const uint4 t = *reinterpret_cast<const uint4*>(sSFT + s * C::kSfBytes + kb * 512 + lane * 16);
         vt[4 * kb] = t.x; vt[4 * kb + 1] = t.y; vt[4 * kb + 2] = t.z; vt[4 * kb + 3] = t.w;
       }
-      if (!mbar_wait(smem_u32(&sf_empty[slot]),
-                     (static_cast<uint32_t>(i / C::kSlots) & 1u) ^ 1u, abort_flag, p.err_word,
-                     kErrWaitSfEmpty))
-        break;
+      // The slot's previous use (stage u = i - kSlots) is consumed once phase u / kStages of
+      // that stage's "empty" completes; the next phase needs this writer's own stage first.
+      if (i >= C::kSlots) {
+        const int u = i - C::kSlots;
+        if (!mbar_wait(smem_u32(&empty[u % C::kStages]), static_cast<uint32_t>(u / C::kStages) & 1u,
+                       abort_flag, p.err_word, kErrWaitSfEmpty))
+          break;
+      }
       tc_fence_after();
       const uint32_t sf_t = lane_base + 128 + slot * C::kSlotCols;
 #pragma unroll
