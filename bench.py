@@ -12,7 +12,9 @@ c4 is the pair-wise 2:4 sparse configuration (the format the tcgen05 .sp MMA exe
 decode-* are the M <= 128 weight-streaming shapes. Under torchrun every rank computes its own
 N-slice of a problem N*world wide (weak scaling, no data-path collective), except c3-16k,
 whose N = 65536 is split over the ranks (strong scaling); --gather also times the optional
-NCCL all-gather of the C shards. Rank 0 prints one JSON line.
+all-gather of the C shards, both as NCCL all-gather + row-major copy after the GEMM and fused
+into the GEMM's epilogue (tiles stored straight into every rank's row-major output over NVLink).
+Rank 0 prints one JSON line.
 
 `value` is device-timed with operands resident in HBM: for M > 128 the L2 is flushed (256 MiB
 write) before every step and CUDA events bracket each launch; decode shapes rotate the weight
@@ -442,7 +444,49 @@ def run_b200(args, rank, world, local_rank):
         gather = {"ms_per_all_gather": g_ms, "bytes_received_per_gpu": moved,
                   "gbs_per_gpu": moved / (g_ms * 1e-3) / 1e9,
                   "ms_row_major_copy": r_ms, "full_shape": [int(full.shape[0]), int(full.shape[1])]}
-        del shards, full
+
+        # The fused form: each rank's epilogue stores its tiles into every rank's row-major
+        # [M][N_total] buffer over NVLink (CUDA IPC mappings) as they complete; a one-word NCCL
+        # all-reduce per step orders all ranks' GEMMs before the result is read. Timed per
+        # step (GEMM with its gather + that all-reduce) like the GEMM alone, L2 flushed.
+        from nvfp4bench_b200.shard import GatheredOutput
+        go = GatheredOutput(M, n_total, out_dtype, dev)
+        if go.n1 - go.n0 != N:
+            raise RuntimeError("shard width differs from the per-rank N")
+        fargs = api.gemm_args(A.packed, A.scales_tc, B.packed, B.scales_tc, M, N, K, go.local,
+                              sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
+                              cta_group=args.cta_group, mode=mode, a_meta=a_meta,
+                              peers=go.peers)
+        for _ in range(max(3, args.warmup)):
+            flush.zero_()
+            api.launch(fargs)
+            go.wait_all()
+        torch.cuda.synchronize()
+        identical = bool(torch.equal(go.full, full))
+        fs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        dist.barrier()
+        for s_, e_ in fs:
+            flush.zero_()
+            s_.record(stream)
+            api.launch(fargs)
+            go.wait_all()
+            e_.record(stream)
+        torch.cuda.synchronize()
+        f_ms = max_over_ranks([sum(s_.elapsed_time(e_) for s_, e_ in fs) / len(fs)], device=dev)[0]
+        go.wait_all()
+        torch.cuda.synchronize()
+        dist.barrier()
+        go.close()
+        gather["fused"] = {
+            "ms_per_step": f_ms,
+            "ms_per_step_unfused": mean_ms + g_ms + r_ms,
+            "tflops": world * flops / (f_ms * 1e-3) / 1e12,
+            "identical_to_nccl_gather": identical,
+            "how": "epilogue TMA stores of each C tile to every rank's row-major buffer "
+                   "(CUDA IPC) + one-word NCCL all-reduce per step",
+        }
+        del shards, full, go
 
     if rank != 0:
         return 0
@@ -533,7 +577,8 @@ def main(argv=None):
     ap.add_argument("--quantize-a", action="store_true",
                     help="each step quantises fp32 A on the GPU before the GEMM (decode layers)")
     ap.add_argument("--gather", action="store_true",
-                    help="also time an all-gather of the C column shards (N > 1)")
+                    help="also time the all-gather of the C column shards (N > 1): NCCL "
+                         "after the GEMM, and fused into the GEMM's epilogue")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time the device steps only (no ladder, e2e, reference-style timing or "
                          "CPU baseline): the command profiled under ncu")

@@ -58,6 +58,13 @@ struct Nvfp4DeviceOperands {
   // before this call on the stream: the decode kernel may then start streaming the weight
   // before that work completes (programmatic dependent launch).
   bool b_static = false;
+  // Row pitch of `d` in elements (0 = N): `d` may be a column slice of a wider matrix.
+  int ldd = 0;
+  // Further destinations of every FP32/BF16 output tile, each addressed like `d` (same row
+  // pitch): typically other GPUs' buffers mapped into this process, so that a column-sharded
+  // GEMM's all-gather of C is done by the epilogue as the tiles complete. At most 7.
+  void* const* d_peers = nullptr;
+  int n_peers = 0;
 };
 
 // src/gemm.h:25-29. Each backend returns true on success; on failure it sets *err (which

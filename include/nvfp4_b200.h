@@ -55,6 +55,17 @@ typedef struct Nvfp4GemmArgs {
   float c_global;
   int c_sf_layout;
   int flags;            /* NVFP4_FLAG_* */
+  /* Row pitch of c in elements (0 = N; FP32/BF16 output): c may be a column slice of a wider
+   * row-major matrix. */
+  int ldc;
+  /* Fused all-gather (no reference counterpart; the reference runs on one GPU): the epilogue
+   * also stores every FP32/BF16 output tile to c_peers[0 .. n_peers-1] (n_peers <= 7), each
+   * addressed like c with the same pitch, typically the other ranks' output buffers mapped
+   * into this process with nvfp4_b200_ipc_open. The tiles cross NVLink as they complete; when
+   * this call's work has completed on `stream`, every destination holds this call's tiles.
+   * Needs a 16-byte aligned c and c_peers[i] and ldc * element size a multiple of 16. */
+  void* const* c_peers;
+  int n_peers;
 } Nvfp4GemmArgs;
 
 /* Nvfp4GemmArgs.flags. B_STATIC: B and its scales are not written by the work enqueued just
@@ -178,6 +189,17 @@ int nvfp4_b200_device_error(int clear, uint32_t* word, char* err, size_t errlen)
  * context stays usable. Returns the device error word in *word. */
 int nvfp4_b200_wait_selftest(uint64_t limit_ns, uint32_t* word, char* err, size_t errlen);
 
+/* CUDA IPC for the fused all-gather (no reference counterpart). nvfp4_b200_ipc_handle exports
+ * the device allocation holding `ptr` as NVFP4_B200_IPC_HANDLE_BYTES opaque bytes plus the
+ * offset of `ptr` inside it; another process on the same node opens it with
+ * nvfp4_b200_ipc_open, which returns that process's address of the same byte (opening an
+ * allocation twice in one process returns the same mapping, reference-counted), and releases
+ * it with nvfp4_b200_ipc_close. The exporting process keeps the allocation alive until every
+ * importer has closed it. */
+enum { NVFP4_B200_IPC_HANDLE_BYTES = 64 };
+int nvfp4_b200_ipc_handle(const void* ptr, void* handle, size_t* offset, char* err, size_t errlen);
+int nvfp4_b200_ipc_open(const void* handle, size_t offset, void** ptr, char* err, size_t errlen);
+int nvfp4_b200_ipc_close(void* ptr, char* err, size_t errlen);
 /* Library version string. */
 const char* nvfp4_b200_version(void);
 

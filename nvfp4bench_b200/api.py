@@ -32,8 +32,10 @@ EXPORTED = [
     "nvfp4_b200_device_error", "nvfp4_b200_wait_selftest", "nvfp4_b200_version",
     "nvfp4_b200_gemm_noalloc", "nvfp4_b200_gemm_noalloc_scratch_bytes", "nvfp4_b200_peak_ex",
     "nvfp4_b200_quantize_ex", "nvfp4_b200_dequantize_ex", "nvfp4_b200_sparse_meta",
-    "nvfp4_b200_sparse_prune", "nvfp4_b200_sparse_compress",
+    "nvfp4_b200_sparse_prune", "nvfp4_b200_sparse_compress", "nvfp4_b200_ipc_handle",
+    "nvfp4_b200_ipc_open", "nvfp4_b200_ipc_close",
 ]
+IPC_HANDLE_BYTES = 64
 
 
 class Nvfp4Error(RuntimeError):
@@ -54,7 +56,8 @@ class GemmArgs(C.Structure):
         ("mode", C.c_int), ("sf_layout", C.c_int), ("out_dtype", C.c_int),
         ("a_meta", C.c_void_p), ("cta_group", C.c_int), ("tile_n", C.c_int),
         ("c_scales", C.c_void_p), ("c_global", C.c_float), ("c_sf_layout", C.c_int),
-        ("flags", C.c_int),
+        ("flags", C.c_int), ("ldc", C.c_int), ("c_peers", C.POINTER(C.c_void_p)),
+        ("n_peers", C.c_int),
     ]
 
 
@@ -94,6 +97,9 @@ def lib():
                                          C.POINTER(C.c_double), C.POINTER(C.c_double), vp, *errs]
         L.nvfp4_b200_device_error.argtypes = [ip, C.POINTER(C.c_uint32), *errs]
         L.nvfp4_b200_wait_selftest.argtypes = [C.c_uint64, C.POINTER(C.c_uint32), *errs]
+        L.nvfp4_b200_ipc_handle.argtypes = [vp, vp, C.POINTER(sz), *errs]
+        L.nvfp4_b200_ipc_open.argtypes = [vp, sz, C.POINTER(vp), *errs]
+        L.nvfp4_b200_ipc_close.argtypes = [vp, *errs]
         L.nvfp4_b200_version.restype = C.c_char_p
         for name in EXPORTED:
             if name not in ("nvfp4_b200_sf_tcgen05_bytes", "nvfp4_b200_version",
@@ -139,13 +145,16 @@ def gemm(a_packed, a_scales, b_packed, b_scales, M: int, N: int, K: int, out: to
          a_global: float = 1.0, b_global: float = 1.0, sf_layout: int = SF_TCGEN05,
          mode: int = MODE_DENSE, a_meta=None, cta_group: int = 0, tile_n: int = 0,
          out_scales=None, out_global: float = 1.0, out_sf_layout: int = SF_CANONICAL,
-         stream=None) -> torch.Tensor:
-    """D = (a_global*b_global) * A @ B^T into `out`: float32 or bfloat16 [M, N], or packed NVFP4
-    uint8 [M, N/2] with `out_scales` (canonical [M, N/16] or tcgen05 layout) and `out_global`."""
+         peers=None, stream=None) -> torch.Tensor:
+    """D = (a_global*b_global) * A @ B^T into `out`: float32 or bfloat16 [M, N] (a column slice
+    of a wider row-major matrix is fine: its row stride is the pitch), or packed NVFP4 uint8
+    [M, N/2] with `out_scales` (canonical [M, N/16] or tcgen05 layout) and `out_global`.
+    `peers`: device addresses (ints) of further destinations that receive every tile, each
+    addressed like `out` with the same pitch (the fused all-gather; see shard.GatheredOutput)."""
     args = gemm_args(a_packed, a_scales, b_packed, b_scales, M, N, K, out, a_global=a_global,
                      b_global=b_global, sf_layout=sf_layout, mode=mode, a_meta=a_meta,
                      cta_group=cta_group, tile_n=tile_n, out_scales=out_scales,
-                     out_global=out_global, out_sf_layout=out_sf_layout)
+                     out_global=out_global, out_sf_layout=out_sf_layout, peers=peers)
     _call(lib().nvfp4_b200_gemm, C.byref(args), _stream(stream))
     return out
 
@@ -153,17 +162,45 @@ def gemm(a_packed, a_scales, b_packed, b_scales, M: int, N: int, K: int, out: to
 def gemm_args(a_packed, a_scales, b_packed, b_scales, M, N, K, out, **kw) -> GemmArgs:
     """Prebuilt argument block for repeated launches (see launch())."""
     od = _out_kind(out, kw.get("out_scales"))
-    return GemmArgs(_ptr(a_packed), _ptr(a_scales), kw.get("a_global", 1.0), _ptr(b_packed),
+    ldc = 0
+    if od != OUT_NVFP4 and out.dim() == 2 and out.stride(1) == 1 and out.stride(0) != N:
+        ldc = out.stride(0)
+    peers = list(kw.get("peers") or [])
+    arr = (C.c_void_p * max(1, len(peers)))(*peers)
+    args = GemmArgs(_ptr(a_packed), _ptr(a_scales), kw.get("a_global", 1.0), _ptr(b_packed),
                     _ptr(b_scales), kw.get("b_global", 1.0), _ptr(out), M, N, K,
                     kw.get("mode", MODE_DENSE), kw.get("sf_layout", SF_TCGEN05), od,
                     _ptr(kw.get("a_meta")), kw.get("cta_group", 0), kw.get("tile_n", 0),
                     _ptr(kw.get("out_scales")), kw.get("out_global", 1.0),
                     kw.get("out_sf_layout", SF_CANONICAL),
-                    FLAG_B_STATIC if kw.get("b_static") else 0)
+                    FLAG_B_STATIC if kw.get("b_static") else 0, ldc,
+                    C.cast(arr, C.POINTER(C.c_void_p)) if peers else None, len(peers))
+    args._peers_keepalive = arr  # the C array must outlive every launch of these arguments
+    return args
 
 
 def launch(args: GemmArgs, stream=None) -> None:
     _call(lib().nvfp4_b200_gemm, C.byref(args), _stream(stream))
+
+
+def ipc_handle(t: torch.Tensor):
+    """(handle bytes, offset) exporting the device allocation that holds `t`'s first byte."""
+    h = C.create_string_buffer(IPC_HANDLE_BYTES)
+    off = C.c_size_t(0)
+    _call(lib().nvfp4_b200_ipc_handle, C.c_void_p(t.data_ptr()), h, C.byref(off))
+    return h.raw, off.value
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """This process's device address of the byte another process exported (see ipc_handle)."""
+    assert len(handle) == IPC_HANDLE_BYTES
+    p = C.c_void_p(0)
+    _call(lib().nvfp4_b200_ipc_open, C.c_char_p(handle), C.c_size_t(offset), C.byref(p))
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _call(lib().nvfp4_b200_ipc_close, C.c_void_p(ptr))
 
 
 def sf_tcgen05_bytes(rows: int, K: int) -> int:

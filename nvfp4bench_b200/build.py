@@ -28,7 +28,8 @@ CLI = os.path.join(BIN_DIR, "nvfp4bench")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
               "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
-LIB_SOURCES = ["gemm_b200.cu", "gemm_noalloc.cu", "gemm_decode.cu", "codec.cu", "roofs.cu", "capi.cu"]
+LIB_SOURCES = ["gemm_b200.cu", "gemm_noalloc.cu", "gemm_decode.cu", "codec.cu", "roofs.cu", "capi.cu",
+               "ipc.cu"]
 
 
 def nvcc() -> str:

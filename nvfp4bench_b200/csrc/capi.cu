@@ -92,6 +92,9 @@ int nvfp4_b200_gemm(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errl
   op.cta_group = a->cta_group;
   op.tile_n = a->tile_n;
   op.b_static = (a->flags & NVFP4_FLAG_B_STATIC) != 0;
+  op.ldd = a->ldc;
+  op.d_peers = a->c_peers;
+  op.n_peers = a->n_peers;
   std::string e;
   if (!launch_gemm_b200(op, static_cast<cudaStream_t>(stream), &e))
     return fail(classify(e), e, err, errlen);
@@ -119,7 +122,10 @@ int nvfp4_b200_gemm_noalloc(const Nvfp4GemmArgs* a, void* stream, char* err, siz
   op.mode = GemmMode::Dense;
   op.sf_layout = SfLayout::Canonical;
   op.out_dtype = a->out_dtype == NVFP4_OUT_BF16 ? OutDType::BF16 : OutDType::F32;
+  if (a->n_peers != 0)
+    return fail(NVFP4_B200_EINVAL, "the no-alloc GEMM does not write peer outputs", err, errlen);
   op.d = a->c;
+  op.ldd = a->ldc;
   op.cta_group = a->cta_group;
   op.tile_n = a->tile_n;
   std::string e;

@@ -133,6 +133,10 @@ struct GemmParams {
   int sfb_rowblocks;    // ceil(N/128)
   int sfa_rowblocks;    // ceil(M/128)
   uint32_t* err_word;
+  // Further destinations of every output tile (TMA-store path only): tensor maps in global
+  // memory, one per destination, with the same coordinates as the C map.
+  const CUtensorMap* peer_maps;
+  int n_peers;
 };
 
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& tm, int& tn) {
@@ -263,6 +267,9 @@ __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, co
   __syncwarp();
   if (lane == 0) {
     tma_store_2d(e.tmap_c, smem_u32(b), col0, e.row0);
+    // The fused all-gather: the same staged chunk to every peer destination (stores over
+    // NVLink by the TMA unit; one commit group covers them all).
+    for (int r = 0; r < p.n_peers; ++r) tma_store_2d(p.peer_maps + r, smem_u32(b), col0, e.row0);
     bulk_commit_group();
   }
   ++e.count;
@@ -646,7 +653,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
     }
-    if (lane == 0) bulk_wait_group<0>();  // stores complete before the CTA's smem goes away
+    if (lane == 0) {
+      bulk_wait_group<0>();  // stores complete before the CTA's smem goes away
+      if (p.n_peers) fence_sc_sys();  // and, for peer destinations, visible system-wide
+    }
     __syncwarp();
   }
 
@@ -943,7 +953,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(empty_l0 + b * 8);
     }
-    if (lane == 0) bulk_wait_group<0>();
+    if (lane == 0) {
+      bulk_wait_group<0>();
+      if (p.n_peers) fence_sc_sys();
+    }
     __syncwarp();
   }
 
@@ -1017,9 +1030,10 @@ bool encode_operand_map(CUtensorMap* map, const void* base, int rows, int K, int
   return true;
 }
 
-// Row-major output [M][N] as a 2-D tensor, box 32 x 32 elements, swizzled to match the
+// Row-major output [M][N] (row pitch `pitch` elements) as a 2-D tensor, box 32 x 32 elements, swizzled to match the
 // epilogue's staging layout (64-byte rows for BF16, 128-byte rows for FP32).
-bool encode_output_map(CUtensorMap* map, void* base, int M, int N, bool bf16, std::string* err) {
+bool encode_output_map(CUtensorMap* map, void* base, int M, int N, long pitch, bool bf16,
+                       std::string* err) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) {
     set_err(err, "cuTensorMapEncodeTiled unavailable from the driver");
@@ -1027,7 +1041,7 @@ bool encode_output_map(CUtensorMap* map, void* base, int M, int N, bool bf16, st
   }
   const size_t es = bf16 ? 2 : 4;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(N * es)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch * es)};
   cuuint32_t box[2] = {32, 32};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
@@ -1048,8 +1062,10 @@ struct MapKey {
   const void* base;
   long rows, cols;
   int box, kind;  // kind: 0 = operand, 1 = BF16 output, 2 = FP32 output, 3 = operand, 64-byte box
+  long pitch = 0;  // outputs: row pitch in elements
   bool operator==(const MapKey& o) const {
-    return base == o.base && rows == o.rows && cols == o.cols && box == o.box && kind == o.kind;
+    return base == o.base && rows == o.rows && cols == o.cols && box == o.box && kind == o.kind &&
+           pitch == o.pitch;
   }
 };
 struct MapCache {
@@ -1075,7 +1091,7 @@ bool cached_map(const MapKey& k, CUtensorMap* out, std::string* err) {
                 ? encode_operand_map(out, k.base, static_cast<int>(k.rows), static_cast<int>(k.cols),
                                      k.box, err, k.kind == 3)
                         : encode_output_map(out, const_cast<void*>(k.base), static_cast<int>(k.rows),
-                                            static_cast<int>(k.cols), k.kind == 1, err);
+                                            static_cast<int>(k.cols), k.pitch, k.kind == 1, err);
   if (!ok) return false;
   std::lock_guard<std::mutex> lk(g_maps.mu);
   const int i = g_maps.next;
@@ -1129,6 +1145,111 @@ DeviceState* device_state(std::string* err) {
     d.init = true;
   }
   return &d;
+}
+
+// Tensor maps of the peer destinations live in device memory (a kernel parameter would not
+// hold seven of them). One small array per distinct set of destinations and shape, built on
+// first use; entries are replaced round-robin (cudaFree synchronises with kernels in flight).
+struct PeerMapsEntry {
+  int dev = -1;
+  std::vector<const void*> ptrs;
+  long rows = 0, cols = 0, pitch = 0;
+  int kind = 0;
+  CUtensorMap* d_maps = nullptr;
+};
+std::vector<PeerMapsEntry> g_peer_maps;
+int g_peer_next = 0;
+constexpr int kPeerMapEntries = 32;
+
+const CUtensorMap* peer_maps(void* const* peers, int n, long rows, long cols, long pitch, int kind,
+                             std::string* err) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    set_err(err, "cudaGetDevice failed");
+    return nullptr;
+  }
+  std::vector<const void*> key(peers, peers + n);
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (const PeerMapsEntry& e : g_peer_maps)
+    if (e.dev == dev && e.ptrs == key && e.rows == rows && e.cols == cols && e.pitch == pitch &&
+        e.kind == kind)
+      return e.d_maps;
+  std::vector<CUtensorMap> maps(n);
+  for (int i = 0; i < n; ++i)
+    if (!encode_output_map(&maps[i], peers[i], static_cast<int>(rows), static_cast<int>(cols), pitch,
+                           kind == 1, err))
+      return nullptr;
+  PeerMapsEntry ne;
+  ne.dev = dev;
+  ne.ptrs = key;
+  ne.rows = rows;
+  ne.cols = cols;
+  ne.pitch = pitch;
+  ne.kind = kind;
+  if (cudaMalloc(&ne.d_maps, sizeof(CUtensorMap) * n) != cudaSuccess ||
+      cudaMemcpy(ne.d_maps, maps.data(), sizeof(CUtensorMap) * n, cudaMemcpyHostToDevice) !=
+          cudaSuccess) {
+    if (ne.d_maps) cudaFree(ne.d_maps);
+    set_err(err, "cudaMalloc/cudaMemcpy of the peer tensor maps failed");
+    return nullptr;
+  }
+  if (static_cast<int>(g_peer_maps.size()) < kPeerMapEntries) {
+    g_peer_maps.push_back(ne);
+  } else {
+    PeerMapsEntry& old = g_peer_maps[g_peer_next];
+    g_peer_next = (g_peer_next + 1) % kPeerMapEntries;
+    int cur = dev;
+    cudaSetDevice(old.dev);
+    cudaFree(old.d_maps);
+    cudaSetDevice(cur);
+    old = ne;
+  }
+  return ne.d_maps;
+}
+
+// Output side of a launch: row pitch, the TMA-store decision, the C tensor map and the peer
+// destinations. Peers need the TMA-store path (FP32/BF16, 16-byte aligned rows).
+bool setup_output(const Nvfp4DeviceOperands& op, GemmParams& p, void* out, CUtensorMap* tc,
+                  std::string* err) {
+  std::memset(tc, 0, sizeof(*tc));
+  p.peer_maps = nullptr;
+  p.n_peers = 0;
+  const long ldc = op.ldd ? op.ldd : op.N;
+  if (ldc < op.N) {
+    set_err(err, "ldc must be at least N");
+    return false;
+  }
+  if (p.out_nvfp4 && ldc != op.N) {
+    set_err(err, "NVFP4 output takes no ldc");
+    return false;
+  }
+  p.ldc = static_cast<int>(ldc);
+  const int esize = p.out_bf16 ? 2 : 4;
+  p.tma_store = (!p.out_nvfp4 && (static_cast<size_t>(ldc) * esize) % 16 == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) & 15) == 0)
+                    ? 1 : 0;
+  if (op.n_peers != 0) {
+    if (op.n_peers < 0 || op.n_peers > 7 || !op.d_peers) {
+      set_err(err, "n_peers must be 0..7 with a c_peers array");
+      return false;
+    }
+    bool aligned = true;
+    for (int i = 0; i < op.n_peers; ++i)
+      aligned = aligned && op.d_peers[i] && (reinterpret_cast<uintptr_t>(op.d_peers[i]) & 15) == 0;
+    if (!p.tma_store || !aligned) {
+      set_err(err, "peer outputs need FP32/BF16 output, 16-byte aligned c and c_peers, and "
+                   "ldc * element size a multiple of 16");
+      return false;
+    }
+  }
+  const int kind = p.out_bf16 ? 1 : 2;
+  if (p.tma_store && !cached_map(MapKey{out, op.M, op.N, 32, kind, ldc}, tc, err)) return false;
+  if (op.n_peers > 0) {
+    p.peer_maps = peer_maps(op.d_peers, op.n_peers, op.M, op.N, ldc, kind, err);
+    if (!p.peer_maps) return false;
+    p.n_peers = op.n_peers;
+  }
+  return true;
 }
 
 template <int BN, bool SP = false>
@@ -1298,7 +1419,8 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   // the MMA's 128-row side, one CTA per SM, split-K over a cluster when the weight has fewer
   // 128-row tiles than there are SMs). An explicit tile shape or SM grouping selects the
   // general kernel.
-  if (op.M <= 128 && op.cta_group == 0 && op.tile_n == 0 && op.out_dtype != OutDType::NVFP4)
+  if (op.M <= 128 && op.cta_group == 0 && op.tile_n == 0 && op.out_dtype != OutDType::NVFP4 &&
+      (op.ldd == 0 || op.ldd == op.N) && op.n_peers == 0)
     return gemm_decode(op, sfa, sfb, out, s, err);
   int bn = op.tile_n;
   const int tiles_m = (op.M + kBM - 1) / kBM;
@@ -1348,14 +1470,7 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   if (!cached_map(MapKey{op.a_packed, op.M, op.K, kBM, 0}, &ta, err)) return false;
   if (!cached_map(MapKey{op.b_packed, op.N, op.K, cg == 2 ? 128 : bn, 0}, &tb, err)) return false;
   CUtensorMap tc;
-  std::memset(&tc, 0, sizeof(tc));
-  const int esize = p.out_bf16 ? 2 : 4;
-  p.tma_store = (!p.out_nvfp4 && (static_cast<size_t>(op.N) * esize) % 16 == 0 &&
-                 (reinterpret_cast<uintptr_t>(out) & 15) == 0)
-                    ? 1 : 0;
-  if (p.tma_store &&
-      !cached_map(MapKey{out, op.M, op.N, 32, p.out_bf16 ? 1 : 2}, &tc, err))
-    return false;
+  if (!setup_output(op, p, out, &tc, err)) return false;
   if (cg == 2) return launch_pair(ta, tb, tc, p, ds, s, err);
   return bn == 256 ? launch_dense<256>(ta, tb, tc, p, ds, s, err)
                    : launch_dense<128>(ta, tb, tc, p, ds, s, err);
@@ -1449,12 +1564,7 @@ bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err
   // Compressed A: [M][K/4] bytes, i.e. a packed operand of K/2 columns, in 64-byte boxes.
   if (!cached_map(MapKey{op.a_packed, op.M, vk, 128, 3}, &ta, err)) return false;
   if (!cached_map(MapKey{op.b_packed, op.N, op.K, 256, 0}, &tb, err)) return false;
-  std::memset(&tc, 0, sizeof(tc));
-  const int esize = p.out_bf16 ? 2 : 4;
-  p.tma_store = (!p.out_nvfp4 && (static_cast<size_t>(op.N) * esize) % 16 == 0 &&
-                 (reinterpret_cast<uintptr_t>(out) & 15) == 0) ? 1 : 0;
-  if (p.tma_store && !cached_map(MapKey{out, op.M, op.N, 32, p.out_bf16 ? 1 : 2}, &tc, err))
-    return false;
+  if (!setup_output(op, p, out, &tc, err)) return false;
   return launch_dense<256, true>(ta, tb, tc, p, ds, s, err);
 }
 

@@ -244,6 +244,9 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int
                "r"(x), "r"(y), "r"(src)
                : "memory");
 }
+// System-scope fence: this thread's completed writes (peer GPUs' memory included) are ordered
+// before anything it, or work that follows the kernel, does next.
+__device__ __forceinline__ void fence_sc_sys() { asm volatile("fence.sc.sys;" ::: "memory"); }
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

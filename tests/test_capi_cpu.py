@@ -4,6 +4,7 @@ import os
 import re
 
 import pytest
+import torch
 
 from nvfp4bench_b200 import api, build
 
@@ -76,3 +77,22 @@ def test_every_export_declares_argtypes():
         if name in ("nvfp4_b200_version",):
             continue
         assert fn.argtypes is not None, name
+
+
+def test_gemm_args_pitch_and_peers_without_gpu(lib):
+    """A column slice gets its row stride as ldc; peers travel as a C array of addresses."""
+    wide = torch.empty((8, 640), dtype=torch.bfloat16)
+    out = wide[:, 128:384]
+    args = api.gemm_args(None, None, None, None, 8, 256, 64, out, peers=[0x1000, 0x2000])
+    assert args.ldc == 640 and args.n_peers == 2
+    assert [args.c_peers[i] for i in range(2)] == [0x1000, 0x2000]
+    plain = api.gemm_args(None, None, None, None, 8, 640, 64, wide)
+    assert plain.ldc == 0 and plain.n_peers == 0 and not plain.c_peers
+
+
+def test_ipc_argument_errors_without_gpu(lib):
+    buf = C.create_string_buffer(256)
+    off = C.c_size_t(0)
+    assert lib.nvfp4_b200_ipc_handle(None, None, C.byref(off), buf, 256) == 1
+    assert lib.nvfp4_b200_ipc_close(C.c_void_p(0x1234), buf, 256) == 1
+    assert b"not returned" in buf.value
