@@ -235,7 +235,6 @@ struct EpiStage {
   uint32_t count;      // chunks stored so far
   const void* tmap_c;
   int row0;            // first row of this warp's 32-row slab
-  int n_peers;         // further destinations of each chunk (GemmParams::peer_maps)
 };
 
 // Scale one 32 x 32 chunk (lane = row) by alpha, write it to a staging buffer in the TMA
@@ -270,8 +269,7 @@ __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, co
     tma_store_2d(e.tmap_c, smem_u32(b), col0, e.row0);
     // The fused all-gather: the same staged chunk to every peer destination (stores over
     // NVLink by the TMA unit; one commit group covers them all).
-    if (e.n_peers)
-      for (int r = 0; r < e.n_peers; ++r) tma_store_2d(p.peer_maps + r, smem_u32(b), col0, e.row0);
+    for (int r = 0; r < p.n_peers; ++r) tma_store_2d(p.peer_maps + r, smem_u32(b), col0, e.row0);
     bulk_commit_group();
   }
   ++e.count;
@@ -624,7 +622,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
     const int row_in_tile = q * 32 + lane;
-    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0, p.n_peers};
+    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0};
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int b = local & 1;
@@ -932,7 +930,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ------------------------------------------------------------------ epilogue (both)
     const int q = warp & 3;
     const int row_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
-    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0, p.n_peers};
+    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0};
     const uint32_t early_l0 = to_leader(&acc_early[0]);
     const uint32_t empty_l0 = to_leader(&acc_empty[0]);
     int local = 0;
