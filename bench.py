@@ -248,7 +248,7 @@ def run_b200(args, rank, world, local_rank):
     gargs = api.gemm_args(A.packed, A.scales_tc, B.packed, B.scales_tc, M, N, K, C,
                           sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
                           cta_group=args.cta_group, mode=mode, a_meta=a_meta,
-                          b_static=args.quantize_a)
+                          b_static=args.quantize_a or args.b_static)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
@@ -285,7 +285,8 @@ def run_b200(args, rank, world, local_rank):
             keep.append((bp, bs))
             rot.append(api.gemm_args(A.packed, A.scales_tc, bp, bs, M, N, K, C,
                                      sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
-                                     cta_group=args.cta_group, b_static=args.quantize_a))
+                                     cta_group=args.cta_group,
+                                     b_static=args.quantize_a or args.b_static))
     step_no = [0]
     # --quantize-a (decode): every step first quantises the fp32 activations A into the tcgen05
     # layout the GEMM reads (the per-call cost of a real decode layer), then runs the GEMM.
@@ -576,6 +577,9 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quantize-a", action="store_true",
                     help="each step quantises fp32 A on the GPU before the GEMM (decode layers)")
+    ap.add_argument("--b-static", action="store_true",
+                    help="pass NVFP4_FLAG_B_STATIC (weights not written by the preceding launch) "
+                         "so a decode GEMM streams its weight while the previous one finishes")
     ap.add_argument("--gather", action="store_true",
                     help="also time the all-gather of the C column shards (N > 1): NCCL "
                          "after the GEMM, and fused into the GEMM's epilogue")
