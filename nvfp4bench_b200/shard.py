@@ -115,7 +115,8 @@ class GatheredOutput:
                 self._flag = torch.zeros(1, dtype=torch.int32, device=self.full.device)
             dist.all_reduce(self._flag, group=self.group)
         else:
-            torch.cuda.synchronize(self.full.device)
+            if self.full.is_cuda:
+                torch.cuda.synchronize(self.full.device)
             dist.barrier(group=self.group)
 
     def close(self) -> None:

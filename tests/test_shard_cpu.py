@@ -63,3 +63,48 @@ def test_sharded_gemm_equals_unsharded_two_gloo_ranks():
         assert p.exitcode == 0
     assert np.array_equal(full, ref)  # column shards are independent: exact
     assert t == [2.0, 10.0]
+
+
+def _gathered_worker(rank, world, port, out_q):
+    """GatheredOutput's host side with the CUDA IPC calls faked: each rank 'exports' its
+    buffer as its rank number and 'maps' peer r at a synthetic address; the peer destinations
+    handed to the GEMM must be those addresses plus this rank's shard offset."""
+    from nvfp4bench_b200 import api
+    from nvfp4bench_b200.shard import GatheredOutput
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    opened, closed = [], []
+    api.ipc_handle = lambda t: (bytes([rank]) * api.IPC_HANDLE_BYTES, 256 * rank)
+    api.ipc_open = lambda h, off: opened.append((h[0], off)) or (0x100000 * (h[0] + 1) + off)
+    api.ipc_close = lambda p: closed.append(p)
+    go = GatheredOutput(64, 1280, torch.bfloat16, "cpu")
+    peers = list(go.peers)
+    go.wait_all()
+    go.close()
+    out_q.put((rank, go.n0, go.n1, tuple(go.local.stride()), go.local.data_ptr() - go.full.data_ptr(),
+               peers, opened, closed))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_gathered_output_peer_addresses_three_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 3
+    procs = [ctx.Process(target=_gathered_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    spans = [shard_bounds(1280, world, r) for r in range(world)]
+    for rank, n0, n1, stride, off, peers, opened, closed in res:
+        assert (n0, n1) == spans[rank]
+        assert stride == (1280, 1) and off == 2 * n0  # the local slice of the row-major buffer
+        others = [r for r in range(world) if r != rank]
+        assert opened == [(r, 256 * r) for r in others]
+        bases = [0x100000 * (r + 1) + 256 * r for r in others]
+        assert peers == [b + 2 * n0 for b in bases]
+        assert closed == bases
