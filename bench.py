@@ -22,7 +22,8 @@ over copies larger than 3x L2 and time the K back-to-back steps with one event p
 launch's prologue overlaps through programmatic dependent launch); max over ranks.
 --quantize-a adds the GPU quantisation of fp32 A to every (decode) step. `e2e` is the same
 metric through the C ABI with pinned host buffers: each step copies the quantised operands
-host->device, launches, and copies C device->host, all inside the timed region.
+host->device, launches, and copies C device->host, all inside the timed region (consecutive
+steps pipelined over three streams, as a serving loop would run them).
 `--impl reference` times the reference's own algorithm for this path on the host cores (the
 CPU restatement of src/reference.cu in oracle/, over dequantised operands) on a bounded
 sample of output rows; it never touches the GPU.
@@ -382,29 +383,53 @@ def run_b200(args, rank, world, local_rank):
     rt = sorted(s_.elapsed_time(e_) for s_, e_ in ev)
     burst_tf, sust_tf = flops / (rt[0] * 1e-3) / 1e12, flops / (rt[len(rt) // 2] * 1e-3) / 1e12
 
-    # e2e through the C ABI with pinned host buffers.
+    # e2e through the C ABI with pinned host buffers: every step copies its quantised operands
+    # host->device, launches, and copies C device->host. Consecutive steps are pipelined the
+    # way a serving loop would run them: host->device copies on one stream, the GEMM on the
+    # launch stream, device->host copies on a third, device buffers doubled, so step i+1's
+    # inputs and step i-1's result cross PCIe (in opposite directions) while step i computes.
     hA, hAs = A.packed.cpu().pin_memory(), A.scales_tc.cpu().pin_memory()
     hB, hBs = B.packed.cpu().pin_memory(), B.scales_tc.cpu().pin_memory()
     hM = a_meta.cpu().pin_memory() if sparse else None
-    hC = torch.empty((M, N), dtype=out_dtype).pin_memory()
-    dA, dAs = torch.empty_like(A.packed), torch.empty_like(A.scales_tc)
-    dB, dBs = torch.empty_like(B.packed), torch.empty_like(B.scales_tc)
-    dM = torch.empty_like(a_meta) if sparse else None
-    dC = torch.empty_like(C)
-    eargs = api.gemm_args(dA, dAs, dB, dBs, M, N, K, dC, sf_layout=api.SF_TCGEN05,
-                          tile_n=args.tile_n, cta_group=args.cta_group, mode=mode, a_meta=dM)
+    hCs = [torch.empty((M, N), dtype=out_dtype).pin_memory() for _ in range(2)]
+    dbuf = []
+    for _ in range(2):
+        d = {"A": torch.empty_like(A.packed), "As": torch.empty_like(A.scales_tc),
+             "B": torch.empty_like(B.packed), "Bs": torch.empty_like(B.scales_tc),
+             "M": torch.empty_like(a_meta) if sparse else None, "C": torch.empty_like(C)}
+        d["args"] = api.gemm_args(d["A"], d["As"], d["B"], d["Bs"], M, N, K, d["C"],
+                                  sf_layout=api.SF_TCGEN05, tile_n=args.tile_n,
+                                  cta_group=args.cta_group, mode=mode, a_meta=d["M"])
+        dbuf.append(d)
     h2d = hA.numel() + hAs.numel() + hB.numel() + hBs.numel() + (hM.numel() if sparse else 0)
     d2h = M * N * out_bytes
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_gemm = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    e2e_i = [0]
 
     def e2e_step():
-        dA.copy_(hA, non_blocking=True)
-        dAs.copy_(hAs, non_blocking=True)
-        dB.copy_(hB, non_blocking=True)
-        dBs.copy_(hBs, non_blocking=True)
-        if sparse:
-            dM.copy_(hM, non_blocking=True)
-        api.launch(eargs)
-        hC.copy_(dC, non_blocking=True)
+        k = e2e_i[0] % 2
+        d, hC = dbuf[k], hCs[k]
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_gemm[k])        # step i-2's GEMM has read these inputs
+            d["A"].copy_(hA, non_blocking=True)
+            d["As"].copy_(hAs, non_blocking=True)
+            d["B"].copy_(hB, non_blocking=True)
+            d["Bs"].copy_(hBs, non_blocking=True)
+            if sparse:
+                d["M"].copy_(hM, non_blocking=True)
+            ev_in[k].record(s_in)
+        stream.wait_event(ev_in[k])
+        stream.wait_event(ev_out[k])           # step i-2's result has left this buffer
+        api.launch(d["args"], stream)
+        ev_gemm[k].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_gemm[k])
+            hC.copy_(d["C"], non_blocking=True)
+            ev_out[k].record(s_out)
+        e2e_i[0] += 1
 
     for _ in range(2):
         e2e_step()
@@ -413,11 +438,15 @@ def run_b200(args, rank, world, local_rank):
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    s_in.wait_event(e0)
     for _ in range(args.steps):
         e2e_step()
+    for k in range(2):
+        stream.wait_event(ev_out[k])
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks([e0.elapsed_time(e1) / args.steps], device=dev)[0]
+    hC = hCs[(e2e_i[0] - 1) % 2]
     if not torch.equal(hC.to(dev), C):
         raise RuntimeError("e2e output differs from the device-resident output")
 
