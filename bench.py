@@ -327,10 +327,10 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    if decode:
-        # A decode step is shorter than the host's launch path: a GPU spin in front lets the
-        # host enqueue every step first, so the events time the device, not the launches.
-        torch.cuda._sleep(args.steps * 100_000)
+    # A GPU spin in front lets the host enqueue every step (flush, events, launch) before the
+    # first one runs, so the events time the device and never a host launch gap: a decode step
+    # is shorter than the host's launch path, and the flush in front of a large step can be too.
+    torch.cuda._sleep(args.steps * (100_000 if decode else 300_000))
     if decode:
         # One event pair around the K back-to-back steps: an event between two launches
         # would stand between them and stop the next one's set-up from overlapping.
