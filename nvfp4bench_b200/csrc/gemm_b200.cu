@@ -239,7 +239,9 @@ struct EpiStage {
 
 // Scale one 32 x 32 chunk (lane = row) by alpha, write it to a staging buffer in the TMA
 // swizzled layout (64-byte swizzle for BF16 rows of 64 bytes, 128-byte for FP32 rows of 128
-// bytes; either way one st.shared.v4 per 16 bytes without bank conflicts) and store it.
+// bytes; either way one st.shared.v4 per 16 bytes without bank conflicts) and store it (and,
+// with kPeers, to every peer destination).
+template <bool kPeers = true>
 __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, const uint32_t (&r)[32],
                                             int col0) {
   const int lane = threadIdx.x & 31;
@@ -269,7 +271,9 @@ __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, co
     tma_store_2d(e.tmap_c, smem_u32(b), col0, e.row0);
     // The fused all-gather: the same staged chunk to every peer destination (stores over
     // NVLink by the TMA unit; one commit group covers them all).
-    for (int r = 0; r < p.n_peers; ++r) tma_store_2d(p.peer_maps + r, smem_u32(b), col0, e.row0);
+    // Compiled out of the kernels launched without peers: the loop alone cost the C2 GEMM 2%.
+    if constexpr (kPeers)
+      for (int r = 0; r < p.n_peers; ++r) tma_store_2d(p.peer_maps + r, smem_u32(b), col0, e.row0);
     bulk_commit_group();
   }
   ++e.count;
@@ -277,7 +281,7 @@ __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, co
 
 // Load CNT chunks of the accumulator with back-to-back tcgen05.ld and one wait, optionally
 // release them (arrive on `early_bar`) as soon as they are in registers, then store them.
-template <int CNT, bool kRemote = false>
+template <int CNT, bool kRemote = false, bool kPeers = true>
 __device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint32_t acc_t,
                                           const int (&cs)[CNT], int row, int col_base,
                                           uint32_t early_bar) {
@@ -296,7 +300,7 @@ __device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint
 #pragma unroll
   for (int g = 0; g < CNT; ++g) {
     if (p.out_nvfp4) store_chunk_nvfp4(p, r[g], row, col_base + cs[g] * 32);
-    else if (p.tma_store) stage_chunk(p, e, r[g], col_base + cs[g] * 32);
+    else if (p.tma_store) stage_chunk<kPeers>(p, e, r[g], col_base + cs[g] * 32);
     else store_chunk(p, r[g], row, col_base + cs[g] * 32);
   }
 }
@@ -304,7 +308,7 @@ __device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint
 // Drain a 256-column accumulator whose first (buffer 1) or last (buffer 0) OV chunks are
 // shared with the other buffer: those chunks first, released on `early_bar` once they are in
 // registers, then the rest.
-template <int OV, bool kRemote>
+template <int OV, bool kRemote, bool kPeers = true>
 __device__ __forceinline__ void drain_overlapped(const GemmParams& p, EpiStage& e, uint32_t acc_t,
                                                  int b, int row, int col_base, uint32_t early_bar) {
   const int o = b ? 0 : 8 - OV;
@@ -312,26 +316,26 @@ __device__ __forceinline__ void drain_overlapped(const GemmParams& p, EpiStage& 
   const int g0[3] = {o, o + 1, o + 2};
   if constexpr (OV == 3) {
     const int g1[3] = {rest, rest + 1, rest + 2}, g2[2] = {rest + 3, rest + 4};
-    epi_group<3, kRemote>(p, e, acc_t, g0, row, col_base, early_bar);
-    epi_group<3>(p, e, acc_t, g1, row, col_base, 0);
-    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
+    epi_group<3, kRemote, kPeers>(p, e, acc_t, g0, row, col_base, early_bar);
+    epi_group<3, false, kPeers>(p, e, acc_t, g1, row, col_base, 0);
+    epi_group<2, false, kPeers>(p, e, acc_t, g2, row, col_base, 0);
     return;
   }
-  epi_group<3>(p, e, acc_t, g0, row, col_base, 0);
+  epi_group<3, false, kPeers>(p, e, acc_t, g0, row, col_base, 0);
   if constexpr (OV == 6) {
     const int g1[3] = {o + 3, o + 4, o + 5}, g2[2] = {rest, rest + 1};
-    epi_group<3, kRemote>(p, e, acc_t, g1, row, col_base, early_bar);
-    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
+    epi_group<3, kRemote, kPeers>(p, e, acc_t, g1, row, col_base, early_bar);
+    epi_group<2, false, kPeers>(p, e, acc_t, g2, row, col_base, 0);
   } else if constexpr (OV == 5) {
     const int g1[2] = {o + 3, o + 4}, g2[2] = {rest, rest + 1}, g3[1] = {rest + 2};
-    epi_group<2, kRemote>(p, e, acc_t, g1, row, col_base, early_bar);
-    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
-    epi_group<1>(p, e, acc_t, g3, row, col_base, 0);
+    epi_group<2, kRemote, kPeers>(p, e, acc_t, g1, row, col_base, early_bar);
+    epi_group<2, false, kPeers>(p, e, acc_t, g2, row, col_base, 0);
+    epi_group<1, false, kPeers>(p, e, acc_t, g3, row, col_base, 0);
   } else {
     const int g1[1] = {o + 3}, g2[2] = {rest, rest + 1}, g3[2] = {rest + 2, rest + 3};
-    epi_group<1, kRemote>(p, e, acc_t, g1, row, col_base, early_bar);
-    epi_group<2>(p, e, acc_t, g2, row, col_base, 0);
-    epi_group<2>(p, e, acc_t, g3, row, col_base, 0);
+    epi_group<1, kRemote, kPeers>(p, e, acc_t, g1, row, col_base, early_bar);
+    epi_group<2, false, kPeers>(p, e, acc_t, g2, row, col_base, 0);
+    epi_group<2, false, kPeers>(p, e, acc_t, g3, row, col_base, 0);
   }
 }
 
@@ -347,7 +351,7 @@ __device__ __forceinline__ void tc_mma_mxf4nvf4_sp(uint32_t d_tmem, uint64_t a_d
       : "memory");
 }
 
-template <int BN, bool SP = false>
+template <int BN, bool SP = false, bool PEERS = false>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_mxf4nvf4_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b,
@@ -640,13 +644,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (C::kOverlap) {
         // The columns shared with the other buffer: buffer 0's chunks 3..7, buffer 1's
         // chunks 0..4. Load them first and release them as soon as they are in registers.
-        drain_overlapped<C::kOverlapChunks, false>(p, e, acc_t, b, row, col_base,
+        drain_overlapped<C::kOverlapChunks, false, PEERS>(p, e, acc_t, b, row, col_base,
                                                    smem_u32(&acc_early[b]));
       } else {
 #pragma unroll
         for (int c = 0; c < C::kChunks; c += 2) {
           const int g[2] = {c, c + 1};
-          epi_group<2>(p, e, acc_t, g, row, col_base, 0);
+          epi_group<2, false, PEERS>(p, e, acc_t, g, row, col_base, 0);
         }
       }
       tc_fence_before();
@@ -655,7 +659,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     if (lane == 0) {
       bulk_wait_group<0>();  // stores complete before the CTA's smem goes away
-      if (p.n_peers) fence_sc_sys();  // and, for peer destinations, visible system-wide
+      if (PEERS && p.n_peers) fence_sc_sys();  // and, for peer destinations, visible system-wide
     }
     __syncwarp();
   }
@@ -1106,7 +1110,7 @@ struct DeviceState {
   bool init = false;
   int sms = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[3] = {false, false, false};
+  bool attr_set[6] = {};  // one-SM kernels: [128, 256, sparse] x [no peers, peers]
   bool pair_attr_set = false;
   int pair_clusters = 0;  // co-resident SM-pair clusters of the pair kernel
   uint32_t* err_word = nullptr;
@@ -1252,14 +1256,13 @@ bool setup_output(const Nvfp4DeviceOperands& op, GemmParams& p, void* out, CUten
   return true;
 }
 
-template <int BN, bool SP = false>
-bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                  const GemmParams& p,
-                  DeviceState* ds, cudaStream_t s, std::string* err) {
+template <int BN, bool SP, bool PEERS>
+bool launch_dense_as(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                     const GemmParams& p, DeviceState* ds, cudaStream_t s, std::string* err) {
   using C = Cfg<BN, SP>;
-  const int idx = SP ? 2 : (BN == 256 ? 1 : 0);
+  const int idx = (SP ? 2 : (BN == 256 ? 1 : 0)) + (PEERS ? 3 : 0);
   if (!ds->attr_set[idx]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_mxf4nvf4_kernel<BN, SP>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_mxf4nvf4_kernel<BN, SP, PEERS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess) {
@@ -1269,13 +1272,21 @@ bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     ds->attr_set[idx] = true;
   }
   int grid = p.num_tiles < ds->sms ? p.num_tiles : ds->sms;
-  gemm_mxf4nvf4_kernel<BN, SP><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, tc, p);
+  gemm_mxf4nvf4_kernel<BN, SP, PEERS><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, tc, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_err(err, std::string("gemm launch: ") + cudaGetErrorString(e));
     return false;
   }
   return true;
+}
+
+// The kernel with the peer stores compiled in only when the call has peer destinations.
+template <int BN, bool SP = false>
+bool launch_dense(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  const GemmParams& p, DeviceState* ds, cudaStream_t s, std::string* err) {
+  return p.n_peers > 0 ? launch_dense_as<BN, SP, true>(ta, tb, tc, p, ds, s, err)
+                       : launch_dense_as<BN, SP, false>(ta, tb, tc, p, ds, s, err);
 }
 
 bool launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
