@@ -195,7 +195,9 @@ int nvfp4_b200_wait_selftest(uint64_t limit_ns, uint32_t* word, char* err, size_
  * nvfp4_b200_ipc_open, which returns that process's address of the same byte (opening an
  * allocation twice in one process returns the same mapping, reference-counted), and releases
  * it with nvfp4_b200_ipc_close. The exporting process keeps the allocation alive until every
- * importer has closed it. */
+ * importer has closed it. The allocation must come from cudaMalloc (PyTorch's default caching
+ * allocator; not expandable segments or other virtual-memory-managed allocations, which
+ * cudaIpcGetMemHandle rejects). */
 enum { NVFP4_B200_IPC_HANDLE_BYTES = 64 };
 int nvfp4_b200_ipc_handle(const void* ptr, void* handle, size_t* offset, char* err, size_t errlen);
 int nvfp4_b200_ipc_open(const void* handle, size_t offset, void** ptr, char* err, size_t errlen);

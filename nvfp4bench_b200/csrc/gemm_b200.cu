@@ -1153,7 +1153,9 @@ DeviceState* device_state(std::string* err) {
 
 // Tensor maps of the peer destinations live in device memory (a kernel parameter would not
 // hold seven of them). One small array per distinct set of destinations and shape, built on
-// first use; entries are replaced round-robin (cudaFree synchronises with kernels in flight).
+// first use and kept for the life of the process (at most 896 bytes each): an array handed to
+// a launch is never freed under it, whichever host thread made the call. Callers that keep
+// making new destination sets (new buffers every call) hit the cap and get an error.
 struct PeerMapsEntry {
   int dev = -1;
   std::vector<const void*> ptrs;
@@ -1162,8 +1164,7 @@ struct PeerMapsEntry {
   CUtensorMap* d_maps = nullptr;
 };
 std::vector<PeerMapsEntry> g_peer_maps;
-int g_peer_next = 0;
-constexpr int kPeerMapEntries = 32;
+constexpr size_t kPeerMapEntries = 4096;
 
 const CUtensorMap* peer_maps(void* const* peers, int n, long rows, long cols, long pitch, int kind,
                              std::string* err) {
@@ -1183,6 +1184,10 @@ const CUtensorMap* peer_maps(void* const* peers, int n, long rows, long cols, lo
     if (!encode_output_map(&maps[i], peers[i], static_cast<int>(rows), static_cast<int>(cols), pitch,
                            kind == 1, err))
       return nullptr;
+  if (g_peer_maps.size() >= kPeerMapEntries) {
+    set_err(err, "too many distinct peer destination sets (keep the peer buffers and reuse them)");
+    return nullptr;
+  }
   PeerMapsEntry ne;
   ne.dev = dev;
   ne.ptrs = key;
@@ -1197,17 +1202,7 @@ const CUtensorMap* peer_maps(void* const* peers, int n, long rows, long cols, lo
     set_err(err, "cudaMalloc/cudaMemcpy of the peer tensor maps failed");
     return nullptr;
   }
-  if (static_cast<int>(g_peer_maps.size()) < kPeerMapEntries) {
-    g_peer_maps.push_back(ne);
-  } else {
-    PeerMapsEntry& old = g_peer_maps[g_peer_next];
-    g_peer_next = (g_peer_next + 1) % kPeerMapEntries;
-    int cur = dev;
-    cudaSetDevice(old.dev);
-    cudaFree(old.d_maps);
-    cudaSetDevice(cur);
-    old = ne;
-  }
+  g_peer_maps.push_back(ne);
   return ne.d_maps;
 }
 
