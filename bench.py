@@ -4,7 +4,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                     [--config c2|c1|c3|c3-16k|c4|decode-{up,down}-{16,64,128}]
-                    [--gather] [--quantize-a] [--kernel-only] [--no-cpu-baseline]
+                    [--gather] [--quantize-a] [--b-static] [--kernel-only]
+                    [--no-cpu-baseline]
 
 One step = one D = A*B^T launch of the workload (config 2 of BASELINE.json by default:
 M=4096 tokens, N=14336, K=4096, N(0,1) operands quantised on the GPU to E2M1/UE4M3, BF16 out).
