@@ -92,6 +92,10 @@ int nvfp4_b200_gemm(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errl
   op.cta_group = a->cta_group;
   op.tile_n = a->tile_n;
   op.b_static = (a->flags & NVFP4_FLAG_B_STATIC) != 0;
+  // Checked before any CUDA call (the engine checks them again with the device-side rules).
+  if (a->ldc != 0 && a->ldc < a->N) return fail(NVFP4_B200_EINVAL, "ldc must be at least N", err, errlen);
+  if (a->n_peers < 0 || a->n_peers > 7 || (a->n_peers > 0 && !a->c_peers))
+    return fail(NVFP4_B200_EINVAL, "n_peers must be 0..7 with a c_peers array", err, errlen);
   op.ldd = a->ldc;
   op.d_peers = a->c_peers;
   op.n_peers = a->n_peers;

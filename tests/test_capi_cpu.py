@@ -96,3 +96,16 @@ def test_ipc_argument_errors_without_gpu(lib):
     assert lib.nvfp4_b200_ipc_handle(None, None, C.byref(off), buf, 256) == 1
     assert lib.nvfp4_b200_ipc_close(C.c_void_p(0x1234), buf, 256) == 1
     assert b"not returned" in buf.value
+
+
+def test_pitch_and_peer_argument_errors_without_gpu(lib):
+    buf = C.create_string_buffer(256)
+    out = torch.empty((8, 256), dtype=torch.bfloat16)
+    args = api.gemm_args(None, None, None, None, 8, 256, 64, out)
+    args.ldc = 128
+    assert lib.nvfp4_b200_gemm(C.byref(args), None, buf, 256) == 1 and b"ldc" in buf.value
+    args = api.gemm_args(None, None, None, None, 8, 256, 64, out, peers=[0x1000] * 8)
+    assert lib.nvfp4_b200_gemm(C.byref(args), None, buf, 256) == 1 and b"n_peers" in buf.value
+    args = api.gemm_args(None, None, None, None, 8, 256, 64, out)
+    args.n_peers = 2  # no array
+    assert lib.nvfp4_b200_gemm(C.byref(args), None, buf, 256) == 1 and b"n_peers" in buf.value
