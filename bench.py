@@ -143,16 +143,18 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------------- reference arm
 def cpu_reference_sample(M, N, K, target_s, threads=0):
-    """Time the oracle (CPU restatement of src/reference.cu:9-17) on a seeded sample of
-    output rows of the workload: returns (tflops, rows, seconds, threads)."""
+    """Time the oracle (CPU restatement of src/reference.cu:9-17) on a seeded sample of the
+    workload: a column slice of at most CPU_MAX_N weight rows and as many output rows as fit in
+    about `target_s` seconds. Returns a dict with the rate and exactly what ran (the FLOPs are
+    counted over the columns that ran, not the workload's full N)."""
     import oracle
     rng = np.random.default_rng(SEED_A)
-    # Host operands of the workload's shape: uniform fill (src/nvfp4.cu:115-129) quantised and
-    # dequantised by the oracle, exactly the values the reference's oracle consumes.
-    a_rows = 64
-    N = min(N, CPU_MAX_N)
-    a = oracle.make_uniform(a_rows, K, SEED_A)
-    b = oracle.make_uniform(N, K, SEED_B)
+    n_cols = min(N, CPU_MAX_N)
+    a_rows = min(M, 256)
+    # N(0,1) operands of the workload's distribution (numpy-seeded), quantised and dequantised
+    # by the oracle: the values the reference's oracle would consume.
+    a = rng.standard_normal((a_rows, K), dtype=np.float32)
+    b = np.random.default_rng(SEED_B).standard_normal((n_cols, K), dtype=np.float32)
     pa, sa = oracle.quantize(a)
     pb, sb = oracle.quantize(b)
     adq = oracle.dequantize(pa, sa, K)
@@ -170,7 +172,13 @@ def cpu_reference_sample(M, N, K, target_s, threads=0):
     t0 = time.perf_counter()
     oracle.gemm_nt_rows(adq, bdq, rows, threads=nthreads)
     dt = time.perf_counter() - t0
-    return 2.0 * n_rows * N * K / dt / 1e12, n_rows, dt, nthreads
+    flops = 2.0 * n_rows * n_cols * K
+    return {"tflops": flops / dt / 1e12, "rows": n_rows, "cols": n_cols, "flops": flops,
+            "seconds": dt, "threads": nthreads, "distinct_rows": a_rows,
+            "sample": (f"{n_rows} output rows (drawn from {a_rows} distinct seeded N(0,1) A rows) "
+                       f"x {n_cols} of {N} cols, K={K}; naive FP32 k-ascending oracle "
+                       f"(src/reference.cu restated) on dequantised NVFP4 operands, "
+                       f"{nthreads} host threads")}
 
 
 def run_reference(args, rank, world):
@@ -179,25 +187,22 @@ def run_reference(args, rank, world):
     if rank != 0:
         return 0
     per_step = []
-    sample_rows = 0
-    cores = 0
     for i in range(args.warmup + args.steps):
-        tf, nr, dt, cores = cpu_reference_sample(M, N, K, target_s=args.ref_step_s)
+        r = cpu_reference_sample(M, N, K, target_s=args.ref_step_s)
         if i >= args.warmup:
-            per_step.append((tf, nr, dt))
-            sample_rows = nr
-    tot_flops = sum(2.0 * nr * N * K for _, nr, _ in per_step)
-    tot_t = sum(dt for _, _, dt in per_step)
+            per_step.append(r)
+    tot_flops = sum(r["flops"] for r in per_step)
+    tot_t = sum(r["seconds"] for r in per_step)
     val = tot_flops / tot_t / 1e12
+    last = per_step[-1]
     line = {
         "impl": "reference", "metric": "nvfp4_gemm_tflops", "value": val, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * tot_t / len(per_step), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": desc, "M": M, "N": N, "K": K},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample_rows} seeded output rows of {M} per step "
-                                   f"(x{N} cols, K={K}); naive FP32 k-ascending oracle"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": last["threads"], "kind": "port",
+                         "sample": "per step: " + last["sample"]},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -558,10 +563,9 @@ def run_b200(args, rank, world, local_rank):
                     "traffic": traffic, "algorithmic_bytes": abytes}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        tf, nr, dt, cores = cpu_reference_sample(M, N, K, target_s=args.cpu_seconds)
-        cpu = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-               "sample": f"{nr} seeded output rows (x{N} cols, K={K}) in {dt:.1f} s; naive FP32 "
-                         f"k-ascending oracle (src/reference.cu restated), all host threads"}
+        r = cpu_reference_sample(M, N, K, target_s=args.cpu_seconds)
+        cpu = {"value": r["tflops"], "unit": "TFLOP/s", "cores": r["threads"], "kind": "port",
+               "sample": f"{r['sample']}; {r['seconds']:.1f} s"}
     line = {
         "metric": "nvfp4_gemm_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_ms,

@@ -16,9 +16,12 @@
 //     tensor cores read scales from Tensor Memory, so no reshuffle is needed per call.
 //   Output: M x N row-major, FP32 into `c` (reference field) or, when `d` is set, the
 //     type `out_dtype` into `d`.
-//   2:4 sparse A (GemmMode::Sparse): a_packed holds the kept values [M][K/4] (two of
-//     every four, in order), a_meta the 2-bit positions of each kept value, a_scales the
-//     scales of the logical (uncompressed) K.
+//   2:4 sparse A (GemmMode::Sparse), the pair-wise form the tcgen05 .sp MMA executes: each
+//     group of 8 consecutive K elements is 4 element pairs of which 2 are kept. a_packed
+//     holds the kept values [M][K/4] (one byte = one kept pair, in order), a_meta [M][K/16]
+//     one nibble per group (first kept pair | second << 2, even group in the low nibble).
+//     A and B scales are one UE4M3 per 32 logical K elements (block 32, not 16): canonical
+//     [rows][K/32], or the tcgen05 layout of nvfp4_b200_sf_tcgen05_bytes(rows, K / 2).
 #pragma once
 
 #include <string>
@@ -48,7 +51,7 @@ struct Nvfp4DeviceOperands {
   void* d = nullptr;                 // output of out_dtype; when null, `c` (FP32) is used
   const uint8_t* a_meta = nullptr;   // 2:4 metadata (GemmMode::Sparse)
   int cta_group = 0;                 // 0 = heuristic, 1 = one-SM tiles, 2 = SM-pair tiles
-  int tile_n = 0;                    // 0 = heuristic, else 64/128/256
+  int tile_n = 0;                    // 0 = heuristic, else 128 or 256 (one-SM dense tiles)
   // NVFP4 output (out_dtype NVFP4): `d` = packed [M][N/2], `d_scales` in d_sf_layout, quantised
   // exactly as quantize_to_nvfp4 (src/nvfp4.cu:62-97) with global scale d_global.
   uint8_t* d_scales = nullptr;

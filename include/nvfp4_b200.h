@@ -46,7 +46,7 @@ typedef struct Nvfp4GemmArgs {
   int out_dtype;        /* NVFP4_OUT_* */
   const void* a_meta;   /* 2:4 metadata, mode == NVFP4_MODE_SPARSE24 only */
   int cta_group;        /* 0 = heuristic, 1 or 2 */
-  int tile_n;           /* 0 = heuristic, else 64, 128 or 256 */
+  int tile_n;           /* 0 = heuristic, else 128 or 256 (one-SM dense tiles) */
   /* out_dtype NVFP4_OUT_NVFP4: c = packed [M][N/2] (N % 32 == 0), c_scales = its UE4M3 scales
    * in c_sf_layout (canonical [M][N/16] or tcgen05, nvfp4_b200_sf_tcgen05_bytes(M, N)),
    * quantised from alpha*acc exactly as quantize_to_nvfp4 (src/nvfp4.cu:62-97) with global
@@ -70,12 +70,19 @@ typedef struct Nvfp4GemmArgs {
 
 /* Nvfp4GemmArgs.flags. B_STATIC: B and its scales are not written by the work enqueued just
  * before this call on the stream, so the decode kernel may start streaming the weight before
- * that work completes (e.g. while this layer's activations are being quantised). */
+ * that work completes (e.g. while this layer's activations are being quantised). It takes
+ * effect only with NVFP4_SF_TCGEN05 scales. */
 enum { NVFP4_FLAG_B_STATIC = 1 };
 
 /* Replaces launch_gemm(KernelKind::Custom, op, s, err) - src/gemm.h:31-40 and the
  * custom backend src/gemm_custom.cu:134-159 - with the tcgen05 backend. With
- * NVFP4_SF_CANONICAL the call reorders the scales into a per-device workspace first. */
+ * NVFP4_SF_CANONICAL the call first reorders the scales into a workspace that belongs to
+ * (device, stream): calls on different streams have separate workspaces, and calls on one
+ * stream are ordered by it, so concurrent canonical-scale calls do not overwrite each other's
+ * scales. The workspace is allocated (cudaMalloc) on a stream's first canonical call and grown
+ * when a larger problem arrives. NVFP4_FLAG_B_STATIC has no effect with canonical scales (the
+ * kernel reads the reordered copy that this call itself writes); use tcgen05-layout scales for
+ * it, and for callers that want no allocation at all. */
 int nvfp4_b200_gemm(const Nvfp4GemmArgs* args, void* stream, char* err, size_t errlen);
 
 /* No counterpart in the reference. Same GEMM as nvfp4_b200_gemm with canonical scales

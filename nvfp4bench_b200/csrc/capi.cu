@@ -111,6 +111,9 @@ int nvfp4_b200_gemm_noalloc(const Nvfp4GemmArgs* a, void* stream, char* err, siz
     return fail(NVFP4_B200_EINVAL, "the no-alloc GEMM supports dense mode only", err, errlen);
   if (a->sf_layout != NVFP4_SF_CANONICAL)
     return fail(NVFP4_B200_EINVAL, "the no-alloc GEMM takes canonical scales", err, errlen);
+  if (a->out_dtype == NVFP4_OUT_NVFP4)
+    return fail(NVFP4_B200_EUNSUPPORTED,
+                "NVFP4 output is not supported by the no-alloc GEMM (FP32 or BF16 only)", err, errlen);
   if (a->out_dtype != NVFP4_OUT_F32 && a->out_dtype != NVFP4_OUT_BF16)
     return fail(NVFP4_B200_EINVAL, "unknown out_dtype", err, errlen);
   Nvfp4DeviceOperands op;

@@ -1114,9 +1114,15 @@ struct DeviceState {
   bool pair_attr_set = false;
   int pair_clusters = 0;  // co-resident SM-pair clusters of the pair kernel
   uint32_t* err_word = nullptr;
-  // Workspace for canonical -> tcgen05 scale reordering (grown on demand).
-  uint8_t* ws = nullptr;
-  size_t ws_bytes = 0;
+  // Workspaces for canonical -> tcgen05 scale reordering, one per stream (grown on demand):
+  // calls on different streams never share reordered scales, and calls on one stream are
+  // ordered by the stream itself.
+  struct Workspace {
+    cudaStream_t stream;
+    uint8_t* ptr;
+    size_t bytes;
+  };
+  std::vector<Workspace> ws;
 };
 
 std::mutex g_mu;
@@ -1333,6 +1339,30 @@ uint32_t* device_error_word(std::string* err) {
   return ds ? ds->err_word : nullptr;
 }
 
+// The scale workspace of stream `s` on this device, at least `bytes` long. Growing it frees
+// the old buffer (cudaFree waits for the device, so earlier work on the stream has finished).
+uint8_t* scale_workspace(DeviceState* ds, cudaStream_t s, size_t bytes, std::string* err) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState::Workspace* w = nullptr;
+  for (auto& x : ds->ws)
+    if (x.stream == s) w = &x;
+  if (!w) {
+    ds->ws.push_back(DeviceState::Workspace{s, nullptr, 0});
+    w = &ds->ws.back();
+  }
+  if (w->bytes < bytes) {
+    if (w->ptr) cudaFree(w->ptr);
+    w->ptr = nullptr;
+    w->bytes = 0;
+    if (cudaMalloc(&w->ptr, bytes) != cudaSuccess) {
+      set_err(err, "cudaMalloc of the scale workspace failed");
+      return nullptr;
+    }
+    w->bytes = bytes;
+  }
+  return w->ptr;
+}
+
 bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err) {
   DeviceState* ds = device_state(err);
   if (!ds) return false;
@@ -1370,23 +1400,21 @@ bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err)
   const uint8_t* sfb = op.b_scales;
   if (op.sf_layout == SfLayout::Canonical) {
     const size_t na = sf_tcgen05_bytes(op.M, op.K), nb = sf_tcgen05_bytes(op.N, op.K);
-    {
-      std::lock_guard<std::mutex> lk(g_mu);
-      if (ds->ws_bytes < na + nb) {
-        if (ds->ws) cudaFree(ds->ws);
-        ds->ws = nullptr;
-        ds->ws_bytes = 0;
-        if (cudaMalloc(&ds->ws, na + nb) != cudaSuccess) {
-          set_err(err, "cudaMalloc of the scale workspace failed");
-          return false;
-        }
-        ds->ws_bytes = na + nb;
-      }
+    uint8_t* ws = scale_workspace(ds, s, na + nb, err);
+    if (!ws) return false;
+    if (!sf_to_tcgen05(op.a_scales, op.M, op.K, ws, s, err)) return false;
+    if (!sf_to_tcgen05(op.b_scales, op.N, op.K, ws + na, s, err)) return false;
+    sfa = ws;
+    sfb = ws + na;
+    // The weight scales the kernel reads were written by the reorder just enqueued, so the
+    // caller's B_STATIC promise does not cover them: the GEMM waits for that work in full.
+    Nvfp4DeviceOperands o = op;
+    o.b_static = false;
+    if ((reinterpret_cast<uintptr_t>(sfa) | reinterpret_cast<uintptr_t>(sfb)) & 15) {
+      set_err(err, "tcgen05-layout scales must be 16-byte aligned");
+      return false;
     }
-    if (!sf_to_tcgen05(op.a_scales, op.M, op.K, ds->ws, s, err)) return false;
-    if (!sf_to_tcgen05(op.b_scales, op.N, op.K, ds->ws + na, s, err)) return false;
-    sfa = ds->ws;
-    sfb = ds->ws + na;
+    return gemm_dense_tc(o, sfa, sfb, out, s, err);
   }
   if ((reinterpret_cast<uintptr_t>(sfa) | reinterpret_cast<uintptr_t>(sfb)) & 15) {
     set_err(err, "tcgen05-layout scales must be 16-byte aligned");
@@ -1523,23 +1551,12 @@ bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err
   const uint8_t* sfb = op.b_scales;
   if (op.sf_layout == SfLayout::Canonical) {
     const size_t na = sf_tcgen05_bytes(op.M, vk), nb = sf_tcgen05_bytes(op.N, vk);
-    {
-      std::lock_guard<std::mutex> lk(g_mu);
-      if (ds->ws_bytes < na + nb) {
-        if (ds->ws) cudaFree(ds->ws);
-        ds->ws = nullptr;
-        ds->ws_bytes = 0;
-        if (cudaMalloc(&ds->ws, na + nb) != cudaSuccess) {
-          set_err(err, "cudaMalloc of the scale workspace failed");
-          return false;
-        }
-        ds->ws_bytes = na + nb;
-      }
-    }
-    if (!sf_to_tcgen05(op.a_scales, op.M, vk, ds->ws, s, err)) return false;
-    if (!sf_to_tcgen05(op.b_scales, op.N, vk, ds->ws + na, s, err)) return false;
-    sfa = ds->ws;
-    sfb = ds->ws + na;
+    uint8_t* ws = scale_workspace(ds, s, na + nb, err);
+    if (!ws) return false;
+    if (!sf_to_tcgen05(op.a_scales, op.M, vk, ws, s, err)) return false;
+    if (!sf_to_tcgen05(op.b_scales, op.N, vk, ws + na, s, err)) return false;
+    sfa = ws;
+    sfb = ws + na;
   }
   if ((reinterpret_cast<uintptr_t>(sfa) | reinterpret_cast<uintptr_t>(sfb)) & 15) {
     set_err(err, "tcgen05-layout scales must be 16-byte aligned");
@@ -1582,6 +1599,11 @@ bool operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_ro
 int device_sms(std::string* err) {
   DeviceState* ds = device_state(err);
   return ds ? ds->sms : 0;
+}
+
+int device_cc_major(std::string* err) {
+  DeviceState* ds = device_state(err);
+  return ds ? ds->cc_major : 0;
 }
 
 bool wait_selftest(uint64_t limit_ns, std::string* err) {

@@ -65,6 +65,16 @@ size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
 size_t noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
 
 bool gemm_noalloc(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err) {
+  const int cc = device_cc_major(err);
+  if (cc == 0) return false;
+  if (cc != 10) {
+    set_err(err, "the b200 backend needs an sm_100 device (found sm_" + std::to_string(cc) + "x)");
+    return false;
+  }
+  if (op.out_dtype == OutDType::NVFP4) {
+    set_err(err, "NVFP4 output is not supported by the no-alloc GEMM (FP32 or BF16 only)");
+    return false;
+  }
   if (op.mode != GemmMode::Dense) {
     set_err(err, "the no-alloc GEMM supports dense mode only");
     return false;

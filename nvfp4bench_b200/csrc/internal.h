@@ -31,6 +31,8 @@ uint32_t* device_error_word(std::string* err);
 bool operand_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows,
                  std::string* err);
 int device_sms(std::string* err);
+// Compute capability major of the current device (0 on error, with *err set).
+int device_cc_major(std::string* err);
 // Weight-streaming GEMM for M <= 128 tokens (gemm_decode.cu); scales in the tcgen05 layout.
 bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb,
                  void* out, cudaStream_t s, std::string* err);

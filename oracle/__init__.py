@@ -27,8 +27,15 @@ _i32p = C.POINTER(C.c_int)
 
 
 def build() -> None:
-    """Compile liborc.so (and _ref/ when the reference source tree exists)."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    """Compile liborc.so, and _ref/ when the reference source tree can be found: the
+    NVFP4BENCH_REF environment variable names the reference project root; unset, a checkout
+    named ``reference`` beside this repository is used when it exists."""
+    env = dict(os.environ)
+    if not env.get("NVFP4BENCH_REF") and not env.get("REF_SRC"):
+        sibling = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+        if os.path.isfile(os.path.join(sibling, "src", "nvfp4.cu")):
+            env["NVFP4BENCH_REF"] = sibling
+    subprocess.run(["make", "-s", "-C", HERE], check=True, env=env)
 
 
 def _load(path: str):

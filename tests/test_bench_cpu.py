@@ -36,3 +36,23 @@ def test_strong_config_shards_evenly():
     for g in (1, 2, 4, 8):
         widths = {n1 - n0 for n0, n1 in (shard_bounds(N, g, r) for r in range(g))}
         assert widths == {N // g}
+
+
+def test_cpu_sample_counts_the_columns_it_ran():
+    # The weight is capped at CPU_MAX_N columns; the FLOPs and the label must use that width.
+    r = bench.cpu_reference_sample(64, bench.CPU_MAX_N + 4096, 256, target_s=0.05, threads=2)
+    assert r["cols"] == bench.CPU_MAX_N
+    assert r["flops"] == 2.0 * r["rows"] * r["cols"] * 256
+    assert abs(r["tflops"] - r["flops"] / r["seconds"] / 1e12) < 1e-12
+    assert f"x {bench.CPU_MAX_N} of {bench.CPU_MAX_N + 4096} cols" in r["sample"]
+    assert r["rows"] <= 64
+
+
+def test_reference_arm_line(capsys):
+    rc = bench.main(["--impl", "reference", "--config", "c1", "--steps", "1", "--warmup", "0",
+                     "--ref-step-s", "0.05"])
+    assert rc == 0
+    import json
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"]["h2d_bytes_per_step"] == 0

@@ -109,3 +109,13 @@ def test_pitch_and_peer_argument_errors_without_gpu(lib):
     args = api.gemm_args(None, None, None, None, 8, 256, 64, out)
     args.n_peers = 2  # no array
     assert lib.nvfp4_b200_gemm(C.byref(args), None, buf, 256) == 1 and b"n_peers" in buf.value
+
+
+def test_noalloc_refuses_nvfp4_output_without_gpu(lib):
+    args = api.GemmArgs()
+    args.mode = api.MODE_DENSE
+    args.sf_layout = api.SF_CANONICAL
+    args.out_dtype = api.OUT_NVFP4
+    buf = C.create_string_buffer(256)
+    assert lib.nvfp4_b200_gemm_noalloc(C.byref(args), None, buf, 256) == 3
+    assert b"NVFP4 output is not supported" in buf.value

@@ -4,8 +4,11 @@ Callers such as CUDA-graph capture, servers that own all device memory through t
 pool, or latency-critical loops cannot let a library cudaMalloc a workspace. This entry point
 reorders the canonical scales into a fixed scratch array compiled into the library instead.
 The test checks its output against the regular entry point (nvfp4_b200_gemm, canonical
-scales), within the suite's GEMM tolerance, on two calls in a row (the second call reuses the
-scratch the first one left behind), and that a problem too large for the scratch is refused.
+scales) on consecutive calls (each later call reuses the scratch the previous one left
+behind). Both entry points run the same kernel on the same bytes, so the outputs must be
+bit-identical, not merely within the suite's GEMM tolerance. One shape has M <= 128, which
+routes through the weight-streaming decode kernel. A problem too large for the scratch and
+NVFP4 output are refused.
 This file is collected last so that a run stopping at the first failure has run all others.
 """
 import ctypes as C
@@ -36,7 +39,8 @@ def _call(fn, args):
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 def test_noalloc_matches_regular_entry_point(api, out_dtype):
     L = api.lib()
-    shapes = [(512, 768, 1024, 5), (300, 520, 288, 6)]  # second call: a different shape
+    # Consecutive calls with different shapes; the third (M <= 128) takes the decode kernel.
+    shapes = [(512, 768, 1024, 5), (300, 520, 288, 6), (64, 768, 1024, 7), (64, 768, 1024, 8)]
     for M, N, K, seed in shapes:
         _, a = make_operand(api, M, K, seed, global_scale=0.5)
         _, b = make_operand(api, N, K, seed + 100, global_scale=2.0)
@@ -51,7 +55,18 @@ def test_noalloc_matches_regular_entry_point(api, out_dtype):
         g = got.float().cpu().numpy().astype(np.float64)
         assert np.isfinite(g).all()
         assert np.abs(g - r).max() <= TOL * np.abs(r).max()
+        assert torch.equal(got, ref), f"{M}x{N}x{K}: no-alloc output differs from nvfp4_b200_gemm"
     assert api.device_error() == 0
+
+
+def test_noalloc_refuses_nvfp4_output(api):
+    L = api.lib()
+    dummy = torch.empty(16, dtype=torch.uint8, device="cuda")
+    args = api.GemmArgs(dummy.data_ptr(), dummy.data_ptr(), 1.0, dummy.data_ptr(),
+                        dummy.data_ptr(), 1.0, dummy.data_ptr(), 128, 128, 128, api.MODE_DENSE,
+                        api.SF_CANONICAL, api.OUT_NVFP4, None, 0, 0)
+    rc, msg = _call(L.nvfp4_b200_gemm_noalloc, args)
+    assert rc == 3 and "NVFP4 output is not supported" in msg
 
 
 def test_noalloc_rejects_oversized_problem(api):
