@@ -192,3 +192,99 @@ def test_decode_b_static_is_identical(api, shape):
         torch.cuda.synchronize()
         assert api.device_error() == 0
         assert torch.equal(out, ref)
+
+
+def _dequant_rows(orc, t, rows):
+    """Dequantise only the given rows of a GPU-quantised operand (canonical scales)."""
+    idx = torch.from_numpy(np.asarray(rows)).long().cuda()
+    p = t.packed[idx].cpu().numpy()
+    s = t.scales[idx].cpu().numpy()
+    return orc.dequantize(p, s, t.cols, t.global_scale)
+
+
+def _tile_rows(M, extra=()):
+    """One row in every 128-row tile row (a different offset in each), plus the given rows."""
+    r = [t * 128 + (t * 37 + 5) % 128 for t in range((M + 127) // 128)]
+    return np.unique(np.concatenate([np.array(r), np.array(extra, dtype=np.int64)])).astype(np.int32)
+
+
+@pytest.mark.parametrize("cta_group", [0, 2])
+def test_c3_8192_cubed_sampled_rows(api, orc, cta_group):
+    """BASELINE config 3 on one GPU (8192^3, BF16 out): a row in every 128-row tile row (so
+    every tile row of the persistent schedule and both accumulator buffers are sampled) plus
+    the matrix edges, over all 8192 columns, against the oracle."""
+    M = N = K = 8192
+    _, a = make_operand(api, M, K, 1234)
+    _, b = make_operand(api, N, K, 1234 ^ 0xABCDEF)
+    c = run_gemm(api, a, b, M, N, K, out_dtype=torch.bfloat16, cta_group=cta_group)
+    rows = _tile_rows(M, extra=(0, 127, 128, 255, 256, M - 1))
+    assert len(rows) >= 64
+    ref = orc.gemm_nt_rows(_dequant_rows(orc, a, rows), oracle_dequant(orc, b),
+                           np.arange(len(rows), dtype=np.int32))
+    check_gemm(c[torch.from_numpy(rows).long().cuda()].float().cpu().numpy(), ref, bf16=True)
+
+
+def test_c3_16k_shard_sampled_rows(api, orc):
+    """One GPU's shard of BASELINE config 3's large case over 8 GPUs: 16384 x (65536/8) x
+    16384, BF16 out; a row in every 128-row tile row, all 8192 columns, against the oracle."""
+    M, N, K = 16384, 65536 // 8, 16384
+    _, a = make_operand(api, M, K, 1234)
+    _, b = make_operand(api, N, K, (1234 ^ 0xABCDEF) + 3)
+    c = run_gemm(api, a, b, M, N, K, out_dtype=torch.bfloat16)
+    rows = _tile_rows(M, extra=(0, M - 1))
+    assert len(rows) >= 128
+    ref = orc.gemm_nt_rows(_dequant_rows(orc, a, rows), oracle_dequant(orc, b),
+                           np.arange(len(rows), dtype=np.int32))
+    check_gemm(c[torch.from_numpy(rows).long().cuda()].float().cpu().numpy(), ref, bf16=True)
+
+
+@pytest.mark.parametrize("out", [torch.float32, torch.bfloat16])
+def test_decode_up_proj_m64(api, orc, out):
+    """BASELINE config 5, up-proj at M = 64 (64 x 14336 x 4096), every output against the
+    oracle."""
+    _case(api, orc, 64, 14336, 4096, seed=64 + 3 * 14336 + 4096, out=out)
+
+
+@pytest.mark.parametrize("shape", [(16, 4096, 14336), (64, 14336, 4096)])
+def test_decode_b_static_with_canonical_scales(api, shape):
+    """With canonical scales the call reorders B's scales itself just before the decode kernel,
+    so B_STATIC must not let the kernel read them early: the output equals the one without
+    the flag, on repeated calls whose reorder rewrites the workspace each time."""
+    M, N, K = shape
+    x, a = make_operand(api, M, K, 81)
+    _, b = make_operand(api, N, K, 82)
+    _, b2 = make_operand(api, N, K, 83)
+    refs = [run_gemm(api, a, bb, M, N, K, sf_layout=api.SF_CANONICAL) for bb in (b, b2)]
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    for i in range(4):
+        bb = (b, b2)[i % 2]
+        g = api.gemm_args(a.packed, a.scales, bb.packed, bb.scales, M, N, K, out,
+                          sf_layout=api.SF_CANONICAL, b_static=True)
+        api.launch(g)
+        torch.cuda.synchronize()
+        assert api.device_error() == 0
+        assert torch.equal(out, refs[i % 2])
+
+
+def test_canonical_calls_on_two_streams(api):
+    """Canonical-scale calls on two streams at once: each stream reorders into its own
+    workspace, so both results equal the serial ones."""
+    shapes = [(512, 1024, 2048), (384, 768, 1024)]
+    ops, refs = [], []
+    for i, (M, N, K) in enumerate(shapes):
+        _, a = make_operand(api, M, K, 90 + i)
+        _, b = make_operand(api, N, K, 95 + i)
+        ops.append((a, b, M, N, K))
+        refs.append(run_gemm(api, a, b, M, N, K, sf_layout=api.SF_CANONICAL))
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [torch.empty((M, N), dtype=torch.float32, device="cuda") for _, _, M, N, _ in ops]
+    torch.cuda.synchronize()
+    for _ in range(3):
+        for (a, b, M, N, K), s, o in zip(ops, streams, outs):
+            with torch.cuda.stream(s):
+                api.gemm(a.packed, a.scales, b.packed, b.scales, M, N, K, o,
+                         sf_layout=api.SF_CANONICAL, stream=s)
+        torch.cuda.synchronize()
+        assert api.device_error() == 0
+        for o, r in zip(outs, refs):
+            assert torch.equal(o, r)
