@@ -5,7 +5,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                     [--config c2|c1|c3|c3-16k|c4|decode-{up,down}-{16,64,128}]
                     [--gather] [--quantize-a] [--b-static] [--kernel-only]
-                    [--no-cpu-baseline]
+                    [--no-cpu-baseline] [--no-extras] [--extra-steps S]
 
 One step = one D = A*B^T launch of the workload (config 2 of BASELINE.json by default:
 M=4096 tokens, N=14336, K=4096, N(0,1) operands quantised on the GPU to E2M1/UE4M3, BF16 out).
@@ -15,7 +15,10 @@ N-slice of a problem N*world wide (weak scaling, no data-path collective), excep
 whose N = 65536 is split over the ranks (strong scaling); --gather also times the optional
 all-gather of the C shards, both as NCCL all-gather + row-major copy after the GEMM and fused
 into the GEMM's epilogue (tiles stored straight into every rank's row-major output over NVLink).
-Rank 0 prints one JSON line.
+Rank 0 prints one JSON line. At N=1 the line also carries `extra`: every other BASELINE
+configuration that fits one GPU (C2 with canonical scales, C3 8192^3, C4, the six decode
+shapes), each timed under the same rules with its own roofline fraction; `gpu_launches`
+counts the headline's timed region only.
 
 `value` is device-timed with operands resident in HBM: for M > 128 the L2 is flushed (256 MiB
 write) before every step and CUDA events bracket each launch; decode shapes rotate the weight
@@ -209,6 +212,125 @@ def run_reference(args, rank, world):
     return 0
 
 
+# ------------------------------------------------------------------------------- extra configs
+# Every other BASELINE configuration that fits one GPU, timed in the default (N=1) run beside
+# the headline: C2 with canonical [rows][K/16] scales (the layout the reference harness hands
+# over, so each call also reorders them), C3 8192^3, C4 and the six decode shapes.
+EXTRA_CONFIGS = ("c2-canonical", "c3", "c4", "decode-up-16", "decode-up-64", "decode-up-128",
+                 "decode-down-16", "decode-down-64", "decode-down-128")
+
+
+def time_extra(api, name, dev, steps, ladder, hbm_gbs):
+    """Operands for workload `name` made and quantised on the GPU, then `steps` timed steps
+    under the headline's rules: M > 128 flushes L2 (256 MiB write) before each step and times
+    it with its own event pair; decode shapes rotate the weight over copies holding >= 3x L2
+    and time the steps back to back. Returns a compact result dict."""
+    import torch
+    canonical = name.endswith("-canonical")
+    cfg = name[: -len("-canonical")] if canonical else name
+    M, N, K, od, desc = CONFIGS[cfg]
+    out_dtype = torch.bfloat16 if od == "bf16" else torch.float32
+    out_bytes = 2 if od == "bf16" else 4
+    sparse = cfg == "c4"
+    x = api.fill_normal(M, K, SEED_A)
+    a_meta = None
+    if sparse:
+        a_meta = api.sparse_meta(M, K, SEED_SPARSE)
+        api.sparse_prune(x, a_meta)
+        A = api.quantize_block(x, 32, canonical=False, tcgen05=True)
+        A.packed = api.sparse_compress(A.packed, a_meta, K)
+    else:
+        A = api.quantize(x, canonical=canonical, tcgen05=not canonical)
+    del x
+    x = api.fill_normal(N, K, SEED_B)
+    B = (api.quantize_block(x, 32, canonical=False, tcgen05=True) if sparse else
+         api.quantize(x, canonical=canonical, tcgen05=not canonical))
+    del x
+    C = torch.empty((M, N), dtype=out_dtype, device=dev)
+    mode = api.MODE_SPARSE24 if sparse else api.MODE_DENSE
+    sfl = api.SF_CANONICAL if canonical else api.SF_TCGEN05
+
+    def scales(t):
+        return t.scales if canonical else t.scales_tc
+
+    decode = M <= 128
+    rot = [api.gemm_args(A.packed, scales(A), B.packed, scales(B), M, N, K, C, sf_layout=sfl,
+                         mode=mode, a_meta=a_meta)]
+    keep = []
+    if decode:
+        wbytes = B.packed.numel() + scales(B).numel()
+        for _ in range(max(2, -(-3 * 126_000_000 // wbytes)) - 1):
+            bp, bs = B.packed.clone(), scales(B).clone()
+            keep.append((bp, bs))
+            rot.append(api.gemm_args(A.packed, scales(A), bp, bs, M, N, K, C, sf_layout=sfl))
+    flush = None if decode else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    i = [0]
+
+    def step():
+        api.launch(rot[i[0] % len(rot)])
+        i[0] += 1
+
+    for _ in range(max(3, 2 * len(rot))):
+        if flush is not None:
+            flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(steps * (100_000 if decode else 300_000))
+    if decode:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+    else:
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for s_, e_ in ev:
+            flush.zero_()
+            s_.record(stream)
+            step()
+            e_.record(stream)
+        torch.cuda.synchronize()
+        ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / steps
+    if api.device_error():
+        raise RuntimeError(f"{name}: device error word set")
+    flops = 2.0 * M * N * K
+    abytes = algorithmic_bytes(M, N, K, out_bytes, sparse)
+    r = {"workload": desc + (" (canonical scales, reordered every call)" if canonical else ""),
+         "M": M, "N": N, "K": K, "ms_per_step": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+         "gbs": abytes / (ms * 1e-3) / 1e9, "algorithmic_bytes": abytes,
+         "gpu_launches_per_step": 3 if canonical else 1,
+         "l2": ("weight rotated over %d copies (> 3x L2)" % len(rot)) if decode else
+               "flushed before every step"}
+    if decode:
+        r["roofline"] = {"bound": "hbm", "peak": hbm_gbs, "unit": "GB/s",
+                         "frac": r["gbs"] / hbm_gbs, "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+    else:
+        key = "sparse_random_burst" if sparse else "random_burst"
+        peak = (ladder.get(key) or {}).get("tflops")
+        r["roofline"] = {"bound": "tensor", "peak": peak, "unit": "TFLOP/s",
+                         "frac": r["tflops"] / peak if peak else None,
+                         "peak_source": "tcgen05 FP4 ladder rung '%s' of this run" % key}
+    del keep, rot, A, B, C, flush
+    torch.cuda.empty_cache()
+    return r
+
+
+def run_extras(api, dev, steps, ladder, hbm_gbs, gpu_index):
+    """Time EXTRA_CONFIGS one after another; one clock record covers them all."""
+    clocks = ClockSampler(gpu_index)
+    clocks.start()
+    time.sleep(0.3)
+    res = {}
+    for name in EXTRA_CONFIGS:
+        res[name] = time_extra(api, name, dev, steps, ladder, hbm_gbs)
+    res["clocks"] = clocks.stop()
+    return res
+
+
 # ------------------------------------------------------------------------------- b200 arm
 def run_b200(args, rank, world, local_rank):
     import torch
@@ -268,7 +390,7 @@ def run_b200(args, rank, world, local_rank):
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         # Burst rungs first: the sustained rung leaves the clock at its power-capped level.
         rungs = [("random_burst", 0x5EED, False, 5, False), ("zero_burst", 0, False, 5, False)]
-        if sparse:
+        if sparse or (world == 1 and not args.no_extras):
             rungs.append(("sparse_random_burst", 0x5EED, False, 5, True))
         rungs.append(("random_sustained", 0x5EED, True, 2000, False))
         for key, seed, sustained, reps, sp in rungs:
@@ -592,6 +714,9 @@ def run_b200(args, rank, world, local_rank):
     }
     if gather is not None:
         line["gather"] = gather
+    if world == 1 and not args.no_extras:
+        line["extra"] = run_extras(api, dev, args.extra_steps, ladder,
+                                   peaks.get("hbm_gbs") or 6650.0, local_rank)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -609,6 +734,9 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-step-s", type=float, default=3.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the other BASELINE configurations timed beside the headline (N=1)")
+    ap.add_argument("--extra-steps", type=int, default=20)
     ap.add_argument("--quantize-a", action="store_true",
                     help="each step quantises fp32 A on the GPU before the GEMM (decode layers)")
     ap.add_argument("--b-static", action="store_true",
