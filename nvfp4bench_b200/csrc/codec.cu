@@ -9,10 +9,10 @@
 //   make_random    :115-129 splitmix64 -> uniform [-1, 1)
 // Every float operation is the same IEEE single operation as in the host code (explicit
 // __fdiv_rn / __fmul_rn, no contraction), so bytes match exactly. The linear 128-way scale
-// search becomes a binary search for the first code whose value is >= x followed by the
-// reference's own error comparison between that code and the one below it: decoded values
-// strictly increase with the code, so the nearest code is one of those two, and an exact
-// tie keeps the lower code as the linear search does.
+// search becomes a rounding of the float's bits to the UE4M3 grid with ties to the lower code
+// (codec_dev.cuh), which picks the same code: decoded values strictly increase with the code,
+// so the nearest code is one of the two grid points around x, and the errors the reference
+// compares are exact float differences there.
 #include <cuda_runtime.h>
 
 #include <string>
@@ -177,24 +177,31 @@ __global__ void sparse_compress_kernel(const uint8_t* __restrict__ packed, const
   }
 }
 
-__global__ void sf_to_tcgen05_kernel(const uint8_t* __restrict__ scales, int rows, int ns, int ka,
-                                     size_t words, uint32_t* __restrict__ out) {
-  for (size_t w = blockIdx.x * size_t(blockDim.x) + threadIdx.x; w < words;
-       w += size_t(gridDim.x) * blockDim.x) {
-    const size_t atom = w >> 7;
-    const int wi = static_cast<int>(w & 127);
-    const int rb = static_cast<int>(atom / ka), kb = static_cast<int>(atom % ka);
-    const int row = rb * 128 + (wi & 3) * 32 + (wi >> 2);
-    uint32_t v = 0;
-    if (row < rows) {
-      const uint8_t* src = scales + static_cast<size_t>(row) * ns;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int s = kb * 4 + i;
-        if (s < ns) v |= static_cast<uint32_t>(src[s]) << (8 * i);
-      }
-    }
-    out[w] = v;
+// One block per (128-row block, 16 scale atoms): the 128 x 64 canonical scale bytes are read
+// row by row (coalesced) into shared memory, then written out as 16 whole 512-byte atoms
+// (coalesced). Rows past `rows` and scales past `ns` are written as zero.
+constexpr int kSfTileAtoms = 16;
+__global__ void __launch_bounds__(256) sf_to_tcgen05_kernel(const uint8_t* __restrict__ scales,
+                                                             int rows, int ns, int ka,
+                                                             uint32_t* __restrict__ out) {
+  __shared__ uint32_t tile[128][kSfTileAtoms + 1];  // [row][atom]: the row's 4 scales of the atom
+  const int rb = blockIdx.y;
+  const int a0 = blockIdx.x * kSfTileAtoms;
+  const int s0 = a0 * 4;
+  uint8_t* tb = reinterpret_cast<uint8_t*>(&tile[0][0]);
+  for (int idx = threadIdx.x; idx < 128 * kSfTileAtoms * 4; idx += blockDim.x) {
+    const int r = idx / (kSfTileAtoms * 4), c = idx % (kSfTileAtoms * 4);
+    const int row = rb * 128 + r, sc = s0 + c;
+    uint8_t v = 0;
+    if (row < rows && sc < ns) v = scales[static_cast<size_t>(row) * ns + sc];
+    tb[(r * (kSfTileAtoms + 1) + c / 4) * 4 + (c & 3)] = v;
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < kSfTileAtoms * 128; w += blockDim.x) {
+    const int a = w >> 7, wi = w & 127;
+    if (a0 + a >= ka) break;
+    const int r = (wi & 3) * 32 + (wi >> 2);
+    out[(static_cast<size_t>(rb) * ka + a0 + a) * 128 + wi] = tile[r][a];
   }
 }
 
@@ -249,7 +256,9 @@ bool quantize_block(const float* src, int rows, int cols, float global_scale, in
   if (nblocks == 0) return true;
   // Block 32: atoms of 128 rows x 4 scales cover 128 K, the same atom layout over cols / 2.
   const int vcols = block == 16 ? cols : cols / 2;
-  if (scales_tc) {
+  // The tcgen05 layout pads rows to 128 and scales to 4 per row: zero it only when there is
+  // padding that the kernel does not write.
+  if (scales_tc && (rows % 128 != 0 || (vcols / 16) % 4 != 0)) {
     if (cudaMemsetAsync(scales_tc, 0, sf_tcgen05_bytes(rows, vcols), s) != cudaSuccess) {
       set_err(err, "cudaMemsetAsync of the tcgen05 scale buffer failed");
       return false;
@@ -359,9 +368,10 @@ bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStr
     set_err(err, "tcgen05 scale output must be 4-byte aligned");
     return false;
   }
-  const size_t words = sf_tcgen05_bytes(rows, K) / 4;
-  sf_to_tcgen05_kernel<<<grid_for(words, 256), 256, 0, s>>>(scales, rows, K / 16, (K + 63) / 64,
-                                                           words, reinterpret_cast<uint32_t*>(out));
+  const int ka = (K + 63) / 64;
+  const dim3 grid((ka + kSfTileAtoms - 1) / kSfTileAtoms, (rows + 127) / 128);
+  sf_to_tcgen05_kernel<<<grid, 256, 0, s>>>(scales, rows, K / 16, ka,
+                                            reinterpret_cast<uint32_t*>(out));
   return check_launch("sf_to_tcgen05", err);
 }
 

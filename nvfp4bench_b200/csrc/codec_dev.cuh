@@ -30,24 +30,40 @@ __device__ __forceinline__ float e4m3_decode_dev(uint8_t code) {
   return (code & 0x80) ? -v : v;
 }
 
+// src/nvfp4.cu:47-59: the nearest code in 0..127 with ties to the lower code, computed from the
+// float's bits. For x >= 2^-6, x = (1 + m/8 + r/2^23) * 2^E lies between code (E+7, m) and the
+// next code up, 2^(E-3) apart; r > 2^19 is strictly nearer the upper one and r == 2^19 is a tie
+// (both errors are exact float differences, the operands being within a factor of two). Below
+// 2^-6 the codes are k/512 apart and x * 512 is exact. x is clamped to 448 (code 126) first, as
+// in the reference; x <= 0 and NaN give 0.
 __device__ __forceinline__ uint8_t e4m3_encode_dev(float x) {
-  if (!(x > 0.0f)) return 0;  // x <= 0 -> 0; NaN -> 0 (no error ever compares smaller)
+  if (!(x > 0.0f)) return 0;
   if (448.0f < x) x = 448.0f;
-  int lo = 1, hi = 126;       // dec(0) = 0 < x and dec(126) = 448 >= x
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (e4m3_decode_pos(mid) >= x) hi = mid; else lo = mid + 1;
+  if (x >= 0.015625f) {
+    const uint32_t b = __float_as_uint(x);
+    const int e = static_cast<int>(b >> 23) - 127;  // -6 .. 8
+    const uint32_t m = (b >> 20) & 7u, r = b & 0xFFFFFu;
+    return static_cast<uint8_t>((((e + 7) << 3) | static_cast<int>(m)) + (r > 0x80000u ? 1 : 0));
   }
-  const float eh = fabsf(__fsub_rn(e4m3_decode_pos(hi), x));
-  const float el = fabsf(__fsub_rn(e4m3_decode_pos(hi - 1), x));
-  return static_cast<uint8_t>(eh < el ? hi : hi - 1);
+  const float f = __fmul_rn(x, 512.0f);
+  const float k = floorf(f);
+  return static_cast<uint8_t>(static_cast<int>(k) + (__fsub_rn(f, k) > 0.5f ? 1 : 0));
 }
 
-// src/nvfp4.cu:18-29, verbatim in structure.
+// src/nvfp4.cu:18-29: the nearest of {0,.5,1,1.5,2,3,4,6}, ties to the smaller magnitude,
+// through float errors |a - mag| compared in order. Below 2^25 that is exactly the count of
+// midpoints {.25,.75,1.25,1.75,2.5,3.5,5} strictly below |x| (checked against the reference's
+// loop over all 2^32 floats); from 2^25 on, rounded errors tie and the loop's order decides, so
+// it runs as written (infinities included). NaN gives 0 either way.
 __device__ __forceinline__ uint8_t e2m1_quantize_dev(float x) {
-  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
   const uint8_t sign = (x < 0.0f) ? 0x8 : 0x0;
   const float a = fabsf(x);
+  if (a < 33554432.0f) {
+    const int i = (a > 0.25f) + (a > 0.75f) + (a > 1.25f) + (a > 1.75f) + (a > 2.5f) + (a > 3.5f) +
+                  (a > 5.0f);
+    return static_cast<uint8_t>(sign | i);
+  }
+  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
   int best = 0;
   float best_err = fabsf(__fsub_rn(a, mag[0]));
 #pragma unroll

@@ -93,3 +93,32 @@ def test_quantize_rejects_bad_shape(api):
     x = torch.zeros((4, 24), device="cuda")
     with pytest.raises(api.Nvfp4Error):
         api.quantize(x)
+
+
+def test_e2m1_midpoints_and_huge_quotients(api, orc):
+    """E2M1 rounding at every midpoint between adjacent magnitudes (+-4 ulps) with an exact
+    unit scale (each block's amax is 6, so the divisor is 1), and blocks whose quotients pass
+    2^25, where the reference's loop over rounded errors decides ties its own way (the scale
+    clamps at 448, so x / 448 reaches that range)."""
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    vals = np.concatenate([(m.view(np.int32) + np.arange(-4, 5, dtype=np.int32)).view(np.float32)
+                           for m in mids])
+    vals = np.concatenate([vals, -vals])
+    nblk = -(-len(vals) // 15)
+    x = np.zeros((nblk, 16), np.float32)
+    x[:, 0] = 6.0
+    flat = np.zeros(nblk * 15, np.float32)
+    flat[:len(vals)] = vals
+    x[:, 1:] = flat.reshape(nblk, 15)
+    huge = np.float32(448.0) * np.array([2.0 ** 25, 2.0 ** 25 * 1.5, 2.0 ** 26, 2.0 ** 30, 3e37 / 448,
+                                         2.0 ** 24, 2.0 ** 25 - 8, 1e6, 7.0, 0.0, 1.0, 2.0 ** 27,
+                                         2.0 ** 25 + 64, 5e36 / 448, 1e30 / 448, 6.0], np.float32)
+    x = np.concatenate([x, huge[None, :], -huge[None, :]])
+    if len(x) % 2:
+        x = np.concatenate([x, np.zeros((1, 16), np.float32)])
+    x = x.reshape(-1, 32)
+    xg = torch.from_numpy(x).cuda()
+    t = api.quantize(xg, 1.0)
+    p, s = orc.quantize(x, 1.0)
+    assert np.array_equal(t.packed.cpu().numpy(), p)
+    assert np.array_equal(t.scales.cpu().numpy(), s)
