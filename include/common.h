@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <string>
+#include <vector>
 
 #include <cuda_runtime.h>
 
@@ -20,6 +21,16 @@
       std::fprintf(stderr, "[CUDA error] %s:%d: %s (%s)\n", __FILE__, __LINE__,        \
                    cudaGetErrorString(_e), #call);                                    \
       std::exit(EXIT_FAILURE);                                                        \
+    }                                                                                 \
+  } while (0)
+
+// src/common.h:23-30 - the harness's non-fatal variant (warns and continues).
+#define CHECK_CUDA_NOEXIT(call)                                                       \
+  do {                                                                                \
+    cudaError_t _e = (call);                                                          \
+    if (_e != cudaSuccess) {                                                          \
+      std::fprintf(stderr, "[CUDA warn] %s:%d: %s (%s)\n", __FILE__, __LINE__,         \
+                   cudaGetErrorString(_e), #call);                                    \
     }                                                                                 \
   } while (0)
 

@@ -99,6 +99,17 @@ def build(verbose: bool = False, force: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"harness build failed:\n{r.stdout}\n{r.stderr}")
+    # The reference's own harness linked against this library,
+    # where the reference tree is at hand; the binary then travels with the repository.
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "nvfp4_refharness", os.path.join(PKG, "refharness", "patch.py"))
+    rh = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(rh)
+    ref = rh.find_reference()
+    if ref and (force or _stale(rh.OUT, [LIB, os.path.join(PKG, "refharness", "patch.py"),
+                                         *headers])):
+        rh.build(ref)
     if logs:
         with open(os.path.join(BUILD, "ptxas.log"), "w") as f:
             for k in sorted(logs):
