@@ -12,9 +12,10 @@ M=4096 tokens, N=14336, K=4096, N(0,1) operands quantised on the GPU to E2M1/UE4
 c4 is the pair-wise 2:4 sparse configuration (the format the tcgen05 .sp MMA executes);
 decode-* are the M <= 128 weight-streaming shapes. Under torchrun every rank computes its own
 N-slice of a problem N*world wide (weak scaling, no data-path collective), except c3-16k,
-whose N = 65536 is split over the ranks (strong scaling); --gather also times the optional
-all-gather of the C shards, both as NCCL all-gather + row-major copy after the GEMM and fused
-into the GEMM's epilogue (tiles stored straight into every rank's row-major output over NVLink).
+whose N = 65536 is split over the ranks (strong scaling). At N > 1 the line also times the
+optional all-gather of the C shards (`gather`; --no-gather skips it), both as NCCL all-gather +
+row-major copy after the GEMM and fused into the GEMM's epilogue (tiles stored straight into
+every rank's row-major output over NVLink), each against the measured NVLink rate.
 Rank 0 prints one JSON line. At N=1 the line also carries `extra`: every other BASELINE
 configuration that fits one GPU (C2 with canonical scales, C3 8192^3, C4, the six decode
 shapes), each timed under the same rules with its own roofline fraction; `gpu_launches`
@@ -72,6 +73,8 @@ SEED_SPARSE = 0x24  # pair pattern of the sparse config
 # Configs whose N is the total over all ranks (strong scaling); the others give every rank its
 # own N-wide slice of a world*N-wide weight (weak scaling).
 STRONG = {"c3-16k"}
+# NVLink peer copy measured on this pool, GB/s per direction per GPU (nominal 900).
+LINK_GBS = 770.0
 # The CPU baseline times a column sample of at most this many weight rows (its rate is per FLOP).
 CPU_MAX_N = 8192
 
@@ -579,7 +582,7 @@ def run_b200(args, rank, world, local_rank):
         raise RuntimeError("e2e output differs from the device-resident output")
 
     gather = None
-    if args.gather and world > 1:
+    if world > 1 and not args.no_gather:
         # The optional exchange: one NCCL all-gather of the C column shards over NVLink, then
         # the optional copy into a row-major [M][N_total] matrix, each timed on its own.
         from nvfp4bench_b200.shard import gather_shards, shards_to_row_major
@@ -636,8 +639,14 @@ def run_b200(args, rank, world, local_rank):
         torch.cuda.synchronize()
         dist.barrier()
         go.close()
+        gather["link_peak_gbs"] = LINK_GBS
+        gather["nccl_link_frac"] = moved / (g_ms * 1e-3) / 1e9 / LINK_GBS
         gather["fused"] = {
             "ms_per_step": f_ms,
+            # Bytes each rank receives over NVLink per step against the link's measured rate:
+            # the fused step cannot beat max(GEMM time, bytes / link rate).
+            "link_frac": moved / (f_ms * 1e-3) / 1e9 / LINK_GBS,
+            "bound": "link" if moved / (LINK_GBS * 1e9) > mean_ms * 1e-3 else "gemm",
             "ms_per_step_unfused": mean_ms + g_ms + r_ms,
             "tflops": world * flops / (f_ms * 1e-3) / 1e12,
             "identical_to_nccl_gather": identical,
@@ -743,8 +752,10 @@ def main(argv=None):
                     help="pass NVFP4_FLAG_B_STATIC (weights not written by the preceding launch) "
                          "so a decode GEMM streams its weight while the previous one finishes")
     ap.add_argument("--gather", action="store_true",
-                    help="also time the all-gather of the C column shards (N > 1): NCCL "
-                         "after the GEMM, and fused into the GEMM's epilogue")
+                    help="time the all-gather of the C column shards (N > 1; the default there): "
+                         "NCCL after the GEMM, and fused into the GEMM's epilogue")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="N > 1: time the weak-scaled GEMM only, without the all-gather legs")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time the device steps only (no ladder, e2e, reference-style timing or "
                          "CPU baseline): the command profiled under ncu")

@@ -8,6 +8,7 @@
 // (the reference's oracle design, src/reference.cu:9-17) using the engine's criterion
 // max|err| <= tol * max|C_ref| next to the reference's max relative error.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 
 #include <algorithm>
 #include <cmath>
@@ -358,6 +359,41 @@ void run_bandwidth() {
 
 }  // namespace
 
+// SM clocks through NVML, reading only (the reference's query_clocks_nvml,
+// src/device_probe.cu:13-32). libnvidia-ml is opened at run time, so the harness neither links
+// nor needs it; the device is matched by PCI bus id, since NVML and CUDA may number devices
+// differently. Returns false when NVML or a query is unavailable.
+static bool nvml_sm_clocks(int cuda_device, int& max_mhz, int& cur_mhz) {
+  void* h = dlopen("libnvidia-ml.so.1", RTLD_LAZY | RTLD_LOCAL);
+  if (!h) return false;
+  using InitFn = int (*)();
+  using ByPciFn = int (*)(const char*, void**);
+  using ClockFn = int (*)(void*, int, unsigned int*);
+  auto init = reinterpret_cast<InitFn>(dlsym(h, "nvmlInit_v2"));
+  auto shutdown = reinterpret_cast<InitFn>(dlsym(h, "nvmlShutdown"));
+  auto by_pci = reinterpret_cast<ByPciFn>(dlsym(h, "nvmlDeviceGetHandleByPciBusId_v2"));
+  auto max_clock = reinterpret_cast<ClockFn>(dlsym(h, "nvmlDeviceGetMaxClockInfo"));
+  auto clock = reinterpret_cast<ClockFn>(dlsym(h, "nvmlDeviceGetClockInfo"));
+  bool ok = false;
+  char bus[32] = {0};
+  if (init && shutdown && by_pci && max_clock && clock &&
+      cudaDeviceGetPCIBusId(bus, sizeof(bus), cuda_device) == cudaSuccess && init() == 0) {
+    void* dev = nullptr;
+    constexpr int kClockSm = 1;  // NVML_CLOCK_SM
+    unsigned int mx = 0, cur = 0;
+    if (by_pci(bus, &dev) == 0) {
+      const bool a = max_clock(dev, kClockSm, &mx) == 0;
+      const bool b = clock(dev, kClockSm, &cur) == 0;
+      if (a) max_mhz = static_cast<int>(mx);
+      if (b) cur_mhz = static_cast<int>(cur);
+      ok = a || b;
+    }
+    shutdown();
+  }
+  dlclose(h);
+  return ok;
+}
+
 int main(int argc, char** argv) {
   std::string kernel_sel = "b200", mode_sel = "dense", csv_path, json_path;
   int m = 4096, n = 14336, k = 4096, device = 0;
@@ -404,6 +440,13 @@ int main(int argc, char** argv) {
   dev.sms = prop.multiProcessorCount;
   std::printf("Device %d: %s, sm_%d%d, %d SMs, %.1f GB, L2 %d MB\n\n", device, prop.name, prop.major,
               prop.minor, prop.multiProcessorCount, prop.totalGlobalMem / 1e9, prop.l2CacheSize >> 20);
+  {
+    int max_mhz = 0, cur_mhz = 0;
+    if (nvml_sm_clocks(device, max_mhz, cur_mhz))
+      std::printf("SM clock (NVML): max %d MHz, current %d MHz\n\n", max_mhz, cur_mhz);
+    else
+      std::printf("SM clock (NVML): unavailable\n\n");
+  }
   if (prop.major != 10) std::printf("warning: this engine targets sm_100 (B200)\n");
   if (do_bw) { run_bandwidth(); std::printf("\n"); }
   if (do_peak) { run_ladder(dev, true); return 0; }

@@ -45,3 +45,15 @@ def test_cli_roofs():
     r = _run(["--peak", "--bandwidth"])
     assert r.returncode == 0, r.stderr
     assert "TFLOPS" in r.stdout and "GB/s" in r.stdout
+
+
+def test_cli_reports_nvml_clocks():
+    """The device line carries the SM clocks read through NVML (reading only), as the
+    reference's probe_device does (src/device_probe.cu:13-32)."""
+    r = _run(["--kernel", "b200", "--m", "256", "--n", "256", "--k", "256", "--iters", "2"])
+    assert r.returncode == 0, r.stdout + r.stderr
+    line = [ln for ln in r.stdout.splitlines() if ln.startswith("SM clock (NVML)")]
+    assert line, r.stdout
+    if "unavailable" not in line[0]:
+        mx = int(line[0].split("max ")[1].split(" MHz")[0])
+        assert 1000 <= mx <= 3000, line[0]
