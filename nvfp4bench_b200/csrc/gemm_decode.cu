@@ -54,6 +54,7 @@ struct DParams {
   int out_bf16;
   int tiles_n, splits, num_kt, ka;
   int b_static;         // the weight may be read before the preceding kernel completes
+  int vec_out;          // C rows and pointer allow 16-byte stores (N * element size % 16 == 0)
   uint32_t* err_word;
 };
 
@@ -317,12 +318,28 @@ __global__ void __launch_bounds__(kDThreads, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");  // before any store of C
     tc_fence_after();
     const uint32_t acc_t = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    // Whole weight tiles with 16-byte-storable rows go through shared memory (the stage ring,
+    // idle once every MMA has completed): each thread writes its row's values token by token
+    // (a warp writes 32 consecutive columns), then the four warps store [token][128 columns]
+    // rows with 16-byte vectors. Thread-per-row scalar stores took ~6 us at M = 128.
+    const bool staged = p.splits == 1 && p.vec_out && (tn + 1) * 128 <= p.N;
+    const int esz = p.out_bf16 ? 2 : 4;
+    uint8_t* tile = smem;  // [MPAD][128] elements of the output type
 #pragma unroll
     for (int c0 = 0; c0 < MPAD; c0 += 32) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(acc_t + c0, r);
       tc_wait_ld();
-      if (p.splits == 1) {
+      if (p.splits == 1 && staged) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          if (c0 + jj >= MPAD) break;
+          const float v = __uint_as_float(r[jj]) * p.alpha;
+          uint8_t* d = tile + (static_cast<size_t>(c0 + jj) * 128 + n_local) * esz;
+          if (p.out_bf16) *reinterpret_cast<__nv_bfloat16*>(d) = __float2bfloat16_rn(v);
+          else *reinterpret_cast<float*>(d) = v;
+        }
+      } else if (p.splits == 1) {
         if (ok && n < p.N) {
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj)
@@ -333,6 +350,19 @@ __global__ void __launch_bounds__(kDThreads, 1)
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj)
           if (c0 + jj < MPAD) part[(c0 + jj) * 128 + n_local] = __uint_as_float(r[jj]);
+      }
+    }
+    if (staged) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+      if (ok) {
+        const int vpr = 128 * esz / 16;  // 16-byte vectors per token row
+        const int tid = threadIdx.x - 64;
+        for (int idx = tid; idx < p.M * vpr; idx += 128) {
+          const int m = idx / vpr, v = idx - m * vpr;
+          const uint4 x = reinterpret_cast<const uint4*>(tile)[idx];
+          *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) +
+                                    (static_cast<size_t>(m) * p.N + tn * 128) * esz + v * 16) = x;
+        }
       }
     }
   }
@@ -370,10 +400,24 @@ __global__ void __launch_bounds__(kDThreads, 1)
             acc.x += v[r].x; acc.y += v[r].y; acc.z += v[r].z; acc.w += v[r].w;
           }
         const int m = idx >> 5, nn = tn * 128 + (idx & 31) * 4;
-        const float o[4] = {acc.x, acc.y, acc.z, acc.w};
+        const float o[4] = {acc.x * p.alpha, acc.y * p.alpha, acc.z * p.alpha, acc.w * p.alpha};
+        if (p.vec_out && nn + 4 <= p.N) {
+          // Four consecutive columns in one 8-byte (BF16) or 16-byte (FP32) store.
+          const size_t off = static_cast<size_t>(m) * p.N + nn;
+          if (p.out_bf16) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]), hi = __floats2bfloat162_rn(o[2], o[3]);
+            uint2 w;
+            w.x = *reinterpret_cast<uint32_t*>(&lo);
+            w.y = *reinterpret_cast<uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + off) = w;
+          } else {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) = make_float4(o[0], o[1], o[2], o[3]);
+          }
+        } else {
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (nn + u < p.N) store_out(p, m, nn + u, o[u] * p.alpha);
+          for (int u = 0; u < 4; ++u)
+            if (nn + u < p.N) store_out(p, m, nn + u, o[u]);
+        }
       }
     }
     // No CTA leaves while a peer may still read its shared memory.
@@ -470,6 +514,11 @@ bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_
   p.ka = (op.K + 63) / 64;
   p.splits = 1;
   p.b_static = op.b_static ? 1 : 0;
+  {
+    const int esz = p.out_bf16 ? 2 : 4;
+    p.vec_out = ((static_cast<size_t>(op.N) * esz) % 16 == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) & 15) == 0) ? 1 : 0;
+  }
   p.err_word = device_error_word(err);
   if (!p.err_word) return false;
   DecodeState* st = nullptr;
