@@ -17,8 +17,8 @@ optional all-gather of the C shards (`gather`; --no-gather skips it), both as NC
 row-major copy after the GEMM and fused into the GEMM's epilogue (tiles stored straight into
 every rank's row-major output over NVLink), each against the measured NVLink rate.
 Rank 0 prints one JSON line. At N=1 the line also carries `extra`: every other BASELINE
-configuration that fits one GPU (C2 with canonical scales, C3 8192^3, C4, the six decode
-shapes), each timed under the same rules with its own roofline fraction; `gpu_launches`
+configuration that fits one GPU (C1, C2 with canonical scales, C3 8192^3, C4, the six
+decode shapes), each timed under the same rules with its own roofline fraction; `gpu_launches`
 counts the headline's timed region only.
 
 `value` is device-timed with operands resident in HBM: for M > 128 the L2 is flushed (256 MiB
@@ -217,9 +217,10 @@ def run_reference(args, rank, world):
 
 # ------------------------------------------------------------------------------- extra configs
 # Every other BASELINE configuration that fits one GPU, timed in the default (N=1) run beside
-# the headline: C2 with canonical [rows][K/16] scales (the layout the reference harness hands
-# over, so each call also reorders them), C3 8192^3, C4 and the six decode shapes.
-EXTRA_CONFIGS = ("c2-canonical", "c3", "c4", "decode-up-16", "decode-up-64", "decode-up-128",
+# the headline: C1 (1024^3, FP32 out), C2 with canonical [rows][K/16] scales (the layout the
+# reference harness hands over, so each call also reorders them), C3 8192^3, C4 and the six
+# decode shapes.
+EXTRA_CONFIGS = ("c1", "c2-canonical", "c3", "c4", "decode-up-16", "decode-up-64", "decode-up-128",
                  "decode-down-16", "decode-down-64", "decode-down-128")
 
 
