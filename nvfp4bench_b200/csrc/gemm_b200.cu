@@ -90,10 +90,14 @@ struct Cfg {
   static constexpr int kBBytes = BN * kBKBytes;                  // 16 / 32 KB
   static constexpr int kStageBytes = kABytes + kBBytes;          // scales bypass smem
   static constexpr int kStages = (BN == 256) ? 4 : 6;
-  static constexpr int kCBufBytes = 32 * 32 * 4;                // one FP32 32 x 32 chunk
-  static constexpr int kCBytes = 4 * 2 * kCBufBytes;            // 4 warps, double-buffered
+  static constexpr int kCBufBytes = 32 * 32 * 4;                // per epilogue warp: 2 BF16 / 1 FP32 chunk
+  static constexpr int kCBytes = 4 * kCBufBytes;                // 4 epilogue warps
+  // Dense: the stage's B scale atoms ((BN / 128) row blocks x 4 K-blocks x 512 bytes), brought
+  // in once per CTA by bulk copy; every scale-writer quadrant reads them from shared memory.
+  static constexpr int kSfbStageBytes = SP ? 0 : ((BN + 127) / 128) * kKBlocksPerStage * 512;
+  static constexpr int kSfbBytes = kStages * kSfbStageBytes;
   static constexpr int kBarBytes = 512;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kSfbBytes + kBarBytes;
   // TMEM: a ring of scale slots at the top (slot it % kSfSlots, freed with the smem stage
   // that used it last), two accumulator buffers below; which 32-column chunks the buffers share.
   static constexpr int kSfSlots = NVFP4_SF_SLOTS;
@@ -245,8 +249,13 @@ template <bool kPeers = true>
 __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, const uint32_t (&r)[32],
                                             int col0) {
   const int lane = threadIdx.x & 31;
-  uint8_t* b = e.buf + (e.count & 1) * 4096;
-  if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer has read it
+  // A warp's 4 KB staging area holds two BF16 chunks (2 KB each, used in turn) or one FP32 chunk.
+  const bool dbl = p.out_bf16 != 0;
+  uint8_t* b = e.buf + (dbl ? (e.count & 1) * 2048 : 0);
+  if (lane == 0) {  // the store that last used this buffer has read it
+    if (dbl) bulk_wait_group_read<1>();
+    else bulk_wait_group_read<0>();
+  }
   __syncwarp();
   if (p.out_bf16) {
 #pragma unroll
@@ -363,14 +372,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = sA + C::kStages * C::kABytes;
   uint8_t* sC = sB + C::kStages * C::kBBytes;  // 1024-aligned: stages are multiples of 1 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sC + C::kCBytes);
+  uint8_t* sSfb = sC + C::kCBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSfb + C::kSfbBytes);
   uint64_t* full = bars;                // A/B bytes + producer + the stage's 4 scale writers
   uint64_t* empty = bars + C::kStages;  // smem stage consumed
   uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* acc_early = acc_full + 4;
   uint64_t* drain = acc_full + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sfb_full = drain + 1;       // dense: the stage's B scale atoms landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sfb_full + C::kStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -387,6 +398,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(smem_u32(&acc_early[b]), 4);
     }
     mbar_init(smem_u32(drain), 1);
+    for (int s = 0; s < C::kStages; ++s) mbar_init(smem_u32(&sfb_full[s]), 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmap_a);
@@ -423,6 +435,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes);
           tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * (SP ? 64 : kBKBytes), m0, fb);
           tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes, n0, fb);
+          if constexpr (!SP) {
+            // The stage's B scale atoms: per 128-row block of B one contiguous run of nkb atoms
+            // (tcgen05 layout), to shared memory at (row block * 4 + K-block) * 512. Row blocks
+            // past the end of B are not copied (the writers store zero scales for them).
+            int nkb = p.ka - kt * kKBlocksPerStage;
+            if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+            int nrb = p.sfb_rowblocks - tn * (BN / 128);
+            if (nrb > BN / 128) nrb = BN / 128;
+            const uint32_t db = smem_u32(&sfb_full[s]);
+            mbar_arrive_expect_tx(db, static_cast<uint32_t>(nrb * nkb * 512));
+            for (int jb = 0; jb < nrb; ++jb)
+              bulk_load(smem_u32(sSfb + s * C::kSfbStageBytes + jb * kKBlocksPerStage * 512),
+                        p.sfb + (static_cast<size_t>(tn * (BN / 128) + jb) * p.ka + kt * kKBlocksPerStage) * 512,
+                        static_cast<uint32_t>(nkb * 512), db);
+          }
         }
       }
       if (!ok) {
@@ -433,6 +460,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const int f = it - back;
           mbar_wait_drain(smem_u32(&full[f % C::kStages]),
                           static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
+          if (!SP)
+            mbar_wait_drain(smem_u32(&sfb_full[f % C::kStages]),
+                            static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
         }
       }
     }
@@ -576,14 +606,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           va[kb] = 0u;
           if (kb < nkb)
             va[kb] = __ldg(reinterpret_cast<const uint32_t*>(ga + q * 4 + (kt * kKBlocksPerStage + kb) * 512));
+        }
+        // B scales from the stage's shared-memory copy (one bulk copy per CTA and stage,
+        // instead of the same 4 KB loaded from L2 by each of the four quadrant writers).
+        if (!mbar_wait(smem_u32(&sfb_full[s]), static_cast<uint32_t>(it / C::kStages) & 1u,
+                       abort_flag, p.err_word, kErrWaitSfFull)) {
+          ok = false;
+          break;
+        }
+        const uint4* sb = reinterpret_cast<const uint4*>(sSfb + s * C::kSfbStageBytes);
+#pragma unroll
+        for (int kb = 0; kb < kKBlocksPerStage; ++kb) {
 #pragma unroll
           for (int jb = 0; jb < C::kSfbAtoms; ++jb) {
             const int rb = tn * (BN / 128) + jb;
             uint4 x = make_uint4(0u, 0u, 0u, 0u);
-            if (kb < nkb && rb < p.sfb_rowblocks)
-              x = __ldg(reinterpret_cast<const uint4*>(
-                  p.sfb + (static_cast<size_t>(rb) * p.ka + kt * kKBlocksPerStage + kb) * 512 +
-                  lane * 16));
+            if (kb < nkb && rb < p.sfb_rowblocks) x = sb[(jb * kKBlocksPerStage + kb) * 32 + lane];
             const int o = kb * C::kSfbColsPerKb + 4 * jb;
             vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
           }
@@ -626,7 +664,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
     const int row_in_tile = q * 32 + lane;
-    EpiStage e{sC + (warp - 2) * 2 * C::kCBufBytes, 0u, &tmap_c, 0};
+    EpiStage e{sC + (warp - 2) * C::kCBufBytes, 0u, &tmap_c, 0};
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int b = local & 1;
