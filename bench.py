@@ -421,22 +421,22 @@ def run_b200(args, rank, world, local_rank):
                                      cta_group=args.cta_group,
                                      b_static=args.quantize_a or args.b_static))
     step_no = [0]
-    # --quantize-a (decode): every step first quantises the fp32 activations A into the tcgen05
-    # layout the GEMM reads (the per-call cost of a real decode layer), then runs the GEMM.
+    # --quantize-a: every step quantises the fp32 activations A into the tcgen05-layout operand
+    # the GEMM reads (the per-call cost of a real decode layer) and runs the GEMM, through
+    # nvfp4_b200_gemm_quantize_a: one fused launch for decode shapes, the quantiser and the GEMM
+    # back to back otherwise.
     xa = None
     if args.quantize_a:
         if sparse:
             raise SystemExit("--quantize-a applies to dense configs")
         xa = api.fill_normal(M, K, SEED_A)
-        qa = api.lib()
-        import ctypes as _C
-        qa_args = (xa.data_ptr(), M, K, _C.c_float(1.0), A.packed.data_ptr(), None,
-                   A.scales_tc.data_ptr())
+    fused_qa = args.quantize_a and decode and K % 64 == 0
 
     def step():
         if xa is not None:
-            api._call(qa.nvfp4_b200_quantize, *qa_args, api._stream(None))
-        api.launch(rot[step_no[0] % len(rot)])
+            api.launch_quantize_a(rot[step_no[0] % len(rot)], xa)
+        else:
+            api.launch(rot[step_no[0] % len(rot)])
         step_no[0] += 1
 
     def before_step():
@@ -712,14 +712,15 @@ def run_b200(args, rank, world, local_rank):
                           if decode else
                           "flushed (256 MiB write) before every step; per-step CUDA events"),
                    "tile_n": args.tile_n or "auto", "sf_layout": "tcgen05",
-                   "step": ("quantise fp32 A (GPU) + GEMM" if args.quantize_a else "GEMM")},
+                   "step": (("quantise fp32 A fused into the GEMM (one launch)" if fused_qa else
+                             "quantise fp32 A (GPU) + GEMM") if args.quantize_a else "GEMM")},
         "burst_tflops": burst_tf, "sustained_tflops": sust_tf,
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
-        "gpu_launches": args.steps * (2 if args.quantize_a else 1),
+        "gpu_launches": args.steps * (2 if args.quantize_a and not fused_qa else 1),
         "clocks": clk,
     }
     if gather is not None:

@@ -85,6 +85,23 @@ enum { NVFP4_FLAG_B_STATIC = 1 };
  * it, and for callers that want no allocation at all. */
 int nvfp4_b200_gemm(const Nvfp4GemmArgs* args, void* stream, char* err, size_t errlen);
 
+/* Activation quantisation fused into the GEMM. The reference quantises both operands on the
+ * host before every run (src/bench.cu:25-32, quantize_to_nvfp4 of src/nvfp4.cu:62-97); a decode
+ * layer instead quantises fresh fp32 activations each step. a_src: fp32 A [M][K] (16-byte
+ * aligned). args->a_packed ([M][K/2]) and args->a_scales (tcgen05 layout,
+ * nvfp4_b200_sf_tcgen05_bytes(M, K)) are OUTPUTS: they receive A quantised with global scale
+ * args->a_global, byte-identical to nvfp4_b200_quantize; then D = A * B^T as nvfp4_b200_gemm
+ * (sf_layout must be NVFP4_SF_TCGEN05, dense). For M <= 128, K % 64 == 0, FP32/BF16 output, no
+ * tile/peer options and a weight of at least half as many 128-row tiles as SMs (so that the
+ * decode kernel splits no K range), this is ONE launch of the weight-streaming kernel: its
+ * CTAs quantise disjoint slices of A, meet at a grid barrier (two counters in device memory,
+ * bounded wait) and only then load the token tiles, while the weight stream starts at once
+ * when NVFP4_FLAG_B_STATIC is set. Fused launches on one device must not overlap on the GPU
+ * (they share the barrier's counters). Other shapes run the quantiser and the GEMM back to
+ * back on the stream (measured faster there). */
+int nvfp4_b200_gemm_quantize_a(const Nvfp4GemmArgs* args, const float* a_src, void* stream,
+                               char* err, size_t errlen);
+
 /* No counterpart in the reference. Same GEMM as nvfp4_b200_gemm with canonical scales
  * (dense mode, sf_layout must be NVFP4_SF_CANONICAL) for callers that cannot let the library
  * allocate device memory: code inside CUDA-graph capture, servers that pre-partition all GPU

@@ -33,7 +33,7 @@ EXPORTED = [
     "nvfp4_b200_gemm_noalloc", "nvfp4_b200_gemm_noalloc_scratch_bytes", "nvfp4_b200_peak_ex",
     "nvfp4_b200_quantize_ex", "nvfp4_b200_dequantize_ex", "nvfp4_b200_sparse_meta",
     "nvfp4_b200_sparse_prune", "nvfp4_b200_sparse_compress", "nvfp4_b200_ipc_handle",
-    "nvfp4_b200_ipc_open", "nvfp4_b200_ipc_close",
+    "nvfp4_b200_ipc_open", "nvfp4_b200_ipc_close", "nvfp4_b200_gemm_quantize_a",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -76,6 +76,7 @@ def lib():
         errs = [C.c_char_p, sz]
         L.nvfp4_b200_gemm.argtypes = [C.POINTER(GemmArgs), vp, *errs]
         L.nvfp4_b200_gemm_noalloc.argtypes = [C.POINTER(GemmArgs), vp, *errs]
+        L.nvfp4_b200_gemm_quantize_a.argtypes = [C.POINTER(GemmArgs), vp, vp, *errs]
         L.nvfp4_b200_gemm_noalloc_scratch_bytes.argtypes = []
         L.nvfp4_b200_gemm_noalloc_scratch_bytes.restype = sz
         L.nvfp4_b200_quantize.argtypes = [vp, ip, ip, C.c_float, vp, vp, vp, vp, *errs]
@@ -181,6 +182,15 @@ def gemm_args(a_packed, a_scales, b_packed, b_scales, M, N, K, out, **kw) -> Gem
 
 def launch(args: GemmArgs, stream=None) -> None:
     _call(lib().nvfp4_b200_gemm, C.byref(args), _stream(stream))
+
+
+def launch_quantize_a(args: GemmArgs, a_src: torch.Tensor, stream=None) -> None:
+    """nvfp4_b200_gemm_quantize_a: quantise fp32 `a_src` [M, K] into args' A buffers (packed and
+    tcgen05 scales, both outputs) and run the GEMM, fused into one launch for decode shapes."""
+    if a_src.dtype != torch.float32 or not a_src.is_contiguous():
+        raise ValueError("a_src must be a contiguous float32 tensor")
+    _call(lib().nvfp4_b200_gemm_quantize_a, C.byref(args), C.c_void_p(a_src.data_ptr()),
+          _stream(stream))
 
 
 def ipc_handle(t: torch.Tensor):

@@ -105,6 +105,66 @@ int nvfp4_b200_gemm(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errl
   return ok(err, errlen);
 }
 
+int nvfp4_b200_gemm_quantize_a(const Nvfp4GemmArgs* a, const float* a_src, void* stream, char* err,
+                               size_t errlen) {
+  if (!a || !a_src) return fail(NVFP4_B200_EINVAL, "null args or a_src", err, errlen);
+  if (a->mode != NVFP4_MODE_DENSE)
+    return fail(NVFP4_B200_EINVAL, "the fused quantisation GEMM is dense only", err, errlen);
+  if (a->sf_layout != NVFP4_SF_TCGEN05)
+    return fail(NVFP4_B200_EINVAL, "the fused quantisation GEMM takes tcgen05-layout scales "
+                "(a_scales is written, b_scales read)", err, errlen);
+  if (!a->a_packed || !a->a_scales)
+    return fail(NVFP4_B200_EINVAL, "a_packed and a_scales (outputs) must be given", err, errlen);
+  if (a->M <= 0 || a->K <= 0 || a->K % 16 != 0)
+    return fail(NVFP4_B200_EINVAL, "M must be positive and K a multiple of 16", err, errlen);
+  bool fused = a->M <= 128 && a->K % 64 == 0 && a->cta_group == 0 && a->tile_n == 0 &&
+               (a->out_dtype == NVFP4_OUT_F32 || a->out_dtype == NVFP4_OUT_BF16) &&
+               (a->ldc == 0 || a->ldc == a->N) && a->n_peers == 0;
+  if (fused) {
+    // The single launch meets at a grid barrier, which costs more than the second launch when
+    // the decode kernel splits K over thread-block clusters (fewer weight tiles than half the
+    // SMs; measured: M=16 down-proj 19.8 us fused, 16.4 us as two launches; up-proj M=16
+    // 13.8 us fused, 14.4 us as two). Fuse only when there is no split.
+    std::string e0;
+    const int sms = nvfp4b200::device_sms(&e0);
+    if (sms <= 0) return fail(NVFP4_B200_ECUDA, e0, err, errlen);
+    fused = static_cast<long>((a->N + 127) / 128) * 2 > sms;
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::string e;
+  if (!fused) {
+    // Any other shape: the standalone quantiser, then the GEMM, on the same stream.
+    if (!nvfp4b200::quantize(a_src, a->M, a->K, a->a_global, static_cast<uint8_t*>(const_cast<void*>(a->a_packed)),
+                             nullptr, static_cast<uint8_t*>(const_cast<void*>(a->a_scales)), s, &e))
+      return fail(classify(e), e, err, errlen);
+    return nvfp4_b200_gemm(a, stream, err, errlen);
+  }
+  const int cc = nvfp4b200::device_cc_major(&e);
+  if (cc == 0) return fail(NVFP4_B200_ECUDA, e, err, errlen);
+  if (cc != 10) return fail(NVFP4_B200_EUNSUPPORTED, "the b200 backend needs an sm_100 device", err, errlen);
+  if (!a->b_packed || !a->b_scales || !a->c) return fail(NVFP4_B200_EINVAL, "null operand pointer", err, errlen);
+  if ((reinterpret_cast<uintptr_t>(a->b_packed) | reinterpret_cast<uintptr_t>(a->b_scales)) & 15)
+    return fail(NVFP4_B200_EINVAL, "B and its scales must be 16-byte aligned", err, errlen);
+  Nvfp4DeviceOperands op;
+  op.a_packed = static_cast<const uint8_t*>(a->a_packed);
+  op.a_scales = static_cast<const uint8_t*>(a->a_scales);
+  op.a_global = a->a_global;
+  op.b_packed = static_cast<const uint8_t*>(a->b_packed);
+  op.b_scales = static_cast<const uint8_t*>(a->b_scales);
+  op.b_global = a->b_global;
+  op.M = a->M;
+  op.N = a->N;
+  op.K = a->K;
+  op.sf_layout = SfLayout::Tcgen05;
+  op.out_dtype = a->out_dtype == NVFP4_OUT_BF16 ? OutDType::BF16 : OutDType::F32;
+  op.d = a->c;
+  op.b_static = (a->flags & NVFP4_FLAG_B_STATIC) != 0;
+  if (!nvfp4b200::gemm_decode_quantize_a(op, a_src, static_cast<uint8_t*>(const_cast<void*>(a->a_scales)),
+                                         static_cast<const uint8_t*>(a->b_scales), a->c, s, &e))
+    return fail(classify(e), e, err, errlen);
+  return ok(err, errlen);
+}
+
 int nvfp4_b200_gemm_noalloc(const Nvfp4GemmArgs* a, void* stream, char* err, size_t errlen) {
   if (!a) return fail(NVFP4_B200_EINVAL, "null args", err, errlen);
   if (a->mode != NVFP4_MODE_DENSE)

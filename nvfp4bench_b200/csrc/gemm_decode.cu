@@ -33,6 +33,7 @@
 #include <vector>
 
 #include "gemm.h"
+#include "codec_dev.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -45,6 +46,22 @@ constexpr int kDSfSlots = 12;     // at most; deep enough that the slot ring nev
 constexpr int kDMaxCluster = 8;
 constexpr int kDSmemBudget = 220 * 1024;
 
+// Grid barrier of the fused quantisation: every CTA's quantiser warps add 1 to `arrive` when
+// their slice of A is written; each producer waits for `arrive` to reach the grid size and
+// then adds 1 to `depart`; the last to depart resets both, so each launch starts from zero.
+// (The next launch on the stream reads them only after this grid has completed.)
+__device__ unsigned int g_qa_arrive = 0;
+__device__ unsigned int g_qa_depart = 0;
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 struct DParams {
   const uint8_t* sfw;   // weight (MMA A side) scales, tcgen05 layout over N rows
   const uint8_t* sft;   // token (MMA B side) scales, tcgen05 layout over M rows
@@ -55,6 +72,13 @@ struct DParams {
   int tiles_n, splits, num_kt, ka;
   int b_static;         // the weight may be read before the preceding kernel completes
   int vec_out;          // C rows and pointer allow 16-byte stores (N * element size % 16 == 0)
+  // Fused activation quantisation (a_src != null): the CTAs first quantise fp32 A [M][K] into
+  // the token operand (packed `a_packed` [M][K/2], tcgen05 scales `sft`) with global scale
+  // a_g, exactly as the standalone quantiser does, then meet at a grid barrier before any
+  // token tile is loaded. The weight stream does not wait for it.
+  const float* a_src;
+  uint8_t* a_packed;
+  float a_g;
   uint32_t* err_word;
 };
 
@@ -160,6 +184,43 @@ __global__ void __launch_bounds__(kDThreads, 1)
   // quantisation of this layer's activations.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
+  if (p.a_src && warp >= 2) {
+    // ------------------------------------------------- fused activation quantisation (phase 1)
+    // Warps 2..9 (idle until the first stage) quantise this CTA's share of the 16-element
+    // blocks of A (src/nvfp4.cu:62-97 through the codec's device code) and write the packed
+    // values and tcgen05-layout scales; scale bytes of the padding rows up to 128 are zeroed,
+    // as the standalone quantiser leaves them.
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // A is the previous kernel's output
+    const int nb = p.K / 16;
+    const long rows_pad = (static_cast<long>(p.M) + 127) / 128 * 128;
+    const long total = rows_pad * nb;
+    const long per = (total + gridDim.x - 1) / gridDim.x;
+    const long b0 = per * blockIdx.x;
+    const long b1 = b0 + per < total ? b0 + per : total;
+    for (long b = b0 + (threadIdx.x - 64); b < b1; b += kDThreads - 64) {
+      const int r = static_cast<int>(b / nb), c = static_cast<int>(b % nb);
+      uint8_t sc = 0;
+      if (r < p.M) {
+        const float4* x4 = reinterpret_cast<const float4*>(p.a_src + static_cast<size_t>(r) * p.K + c * 16);
+        float x[16];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 t = x4[v];
+          x[4 * v] = t.x; x[4 * v + 1] = t.y; x[4 * v + 2] = t.z; x[4 * v + 3] = t.w;
+        }
+        uint32_t lo, hi;
+        sc = quantize16_dev(x, p.a_g, lo, hi);
+        *reinterpret_cast<uint2*>(p.a_packed + (static_cast<size_t>(r) * p.K + c * 16) / 2) = make_uint2(lo, hi);
+      }
+      const size_t atom = static_cast<size_t>(r / 128) * p.ka + c / 4;
+      const_cast<uint8_t*>(p.sft)[atom * 512 + (r % 32) * 16 + ((r / 32) % 4) * 4 + (c % 4)] = sc;
+    }
+    fence_proxy_async_global();  // the token tiles are read back by TMA (async proxy)
+    __threadfence();
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    if (threadIdx.x == 64) atomicAdd(&g_qa_arrive, 1u);
+  }
+
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
@@ -199,9 +260,28 @@ __global__ void __launch_bounds__(kDThreads, 1)
         for (int q2 = 0; q2 < pre; ++q2) issue_w(kt0 + q2, q2);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int q2 = 0; q2 < pre; ++q2) issue_t(kt0 + q2, q2);
+      if (p.a_src) {
+        // Phase 2 of the fused quantisation: every CTA's slice of A is written.
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu(&g_qa_arrive) < gridDim.x) {
+          __nanosleep(64);
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicOr(p.err_word, kErrWaitTmaFull);
+            ok = false;
+            break;
+          }
+        }
+        fence_proxy_async_global();
+        if (atomicAdd(&g_qa_depart, 1u) == gridDim.x - 1) {
+          atomicExch(&g_qa_arrive, 0u);
+          atomicExch(&g_qa_depart, 0u);
+        }
+      }
+      if (ok)
+        for (int q2 = 0; q2 < pre; ++q2) issue_t(kt0 + q2, q2);
       i = pre;
-      for (int kt = kt0 + pre; kt < kt1; ++kt, ++i) {
+      for (int kt = kt0 + pre; kt < kt1 && ok; ++kt, ++i) {
         const int s = i % C::kStages;
         const uint32_t j = static_cast<uint32_t>(i / C::kStages);
         if (!mbar_wait(smem_u32(&empty[s]), (j & 1u) ^ 1u, abort_flag, p.err_word,
@@ -487,10 +567,8 @@ bool launch_decode(const CUtensorMap& tw, const CUtensorMap& tt, DParams p, int 
   return true;
 }
 
-}  // namespace
-
-bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb, void* out,
-                 cudaStream_t s, std::string* err) {
+bool decode_impl(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb, void* out,
+                 const float* a_src, cudaStream_t s, std::string* err) {
   if (op.M > 128) {
     set_err(err, "decode kernel needs M <= 128");
     return false;
@@ -514,6 +592,9 @@ bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_
   p.ka = (op.K + 63) / 64;
   p.splits = 1;
   p.b_static = op.b_static ? 1 : 0;
+  p.a_src = a_src;
+  p.a_packed = const_cast<uint8_t*>(op.a_packed);
+  p.a_g = op.a_global;
   {
     const int esz = p.out_bf16 ? 2 : 4;
     p.vec_out = ((static_cast<size_t>(op.N) * esz) % 16 == 0 &&
@@ -536,6 +617,30 @@ bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_
     case 64: return launch_decode<64>(tw, tt, p, sms, *st, 2, s, err);
     default: return launch_decode<128>(tw, tt, p, sms, *st, 3, s, err);
   }
+}
+
+}  // namespace
+
+bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb, void* out,
+                 cudaStream_t s, std::string* err) {
+  return decode_impl(op, sfa, sfb, out, nullptr, s, err);
+}
+
+// Activation quantisation fused into the decode GEMM (no reference counterpart; the reference
+// quantises on the host before every run, src/bench.cu:25-32): fp32 A [M][K] is quantised into
+// op.a_packed and the tcgen05 scales `sfa` (both outputs, byte-identical to quantize()) and
+// multiplied by B in one launch. M <= 128, K % 64 == 0, B scales in the tcgen05 layout. The
+// kernel's grid barrier uses two counters in device memory: launches of this entry on one
+// device must not overlap.
+bool gemm_decode_quantize_a(const Nvfp4DeviceOperands& op, const float* a_src, uint8_t* sfa,
+                            const uint8_t* sfb, void* out, cudaStream_t s, std::string* err) {
+  if (!a_src || (reinterpret_cast<uintptr_t>(a_src) & 15) || op.K % 64 != 0 || op.M > 128 ||
+      (reinterpret_cast<uintptr_t>(op.a_packed) & 15) || (reinterpret_cast<uintptr_t>(sfa) & 15)) {
+    set_err(err, "fused quantisation needs a 16-byte aligned fp32 A, M <= 128, K % 64 == 0 and "
+                 "16-byte aligned A outputs");
+    return false;
+  }
+  return decode_impl(op, sfa, sfb, out, a_src, s, err);
 }
 
 }  // namespace nvfp4b200

@@ -36,6 +36,10 @@ int device_cc_major(std::string* err);
 // Weight-streaming GEMM for M <= 128 tokens (gemm_decode.cu); scales in the tcgen05 layout.
 bool gemm_decode(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint8_t* sfb,
                  void* out, cudaStream_t s, std::string* err);
+// Decode GEMM with the quantisation of fp32 A fused in (gemm_decode.cu): A's packed values go
+// to op.a_packed and its tcgen05 scales to sfa.
+bool gemm_decode_quantize_a(const Nvfp4DeviceOperands& op, const float* a_src, uint8_t* sfa,
+                            const uint8_t* sfb, void* out, cudaStream_t s, std::string* err);
 bool wait_selftest(uint64_t limit_ns, std::string* err);
 
 // ---- codecs (codec.cu) ---------------------------------------------------------------
