@@ -92,9 +92,12 @@ struct Cfg {
   static constexpr int kStages = (BN == 256) ? 4 : 6;
   static constexpr int kCBufBytes = 32 * 32 * 4;                // per epilogue warp: 2 BF16 / 1 FP32 chunk
   static constexpr int kCBytes = 4 * kCBufBytes;                // 4 epilogue warps
-  // Dense: the stage's B scale atoms ((BN / 128) row blocks x 4 K-blocks x 512 bytes), brought
-  // in once per CTA by bulk copy; every scale-writer quadrant reads them from shared memory.
-  static constexpr int kSfbStageBytes = SP ? 0 : ((BN + 127) / 128) * kKBlocksPerStage * 512;
+  // The stage's B scale atoms ((BN / 128) row blocks x the stage's atoms along K x 512 bytes),
+  // brought in once per CTA by bulk copy; every scale-writer quadrant reads them from shared
+  // memory.
+  // (Sparse: the scale atoms along K are per 128 logical K, two per stage.)
+  static constexpr int kSfbAtomsPerStage = SP ? 2 : kKBlocksPerStage;
+  static constexpr int kSfbStageBytes = ((BN + 127) / 128) * kSfbAtomsPerStage * 512;
   static constexpr int kSfbBytes = kStages * kSfbStageBytes;
   static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kSfbBytes + kBarBytes;
@@ -435,19 +438,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           mbar_arrive_expect_tx(fb, C::kABytes + C::kBBytes);
           tma_load_2d(smem_u32(sA + s * C::kABytes), &tmap_a, kt * (SP ? 64 : kBKBytes), m0, fb);
           tma_load_2d(smem_u32(sB + s * C::kBBytes), &tmap_b, kt * kBKBytes, n0, fb);
-          if constexpr (!SP) {
+          {
             // The stage's B scale atoms: per 128-row block of B one contiguous run of nkb atoms
-            // (tcgen05 layout), to shared memory at (row block * 4 + K-block) * 512. Row blocks
-            // past the end of B are not copied (the writers store zero scales for them).
-            int nkb = p.ka - kt * kKBlocksPerStage;
-            if (nkb > kKBlocksPerStage) nkb = kKBlocksPerStage;
+            // (tcgen05 layout), to shared memory at (row block * atoms per stage + atom) * 512.
+            // Row blocks past the end of B are not copied (the writers store zero scales).
+            constexpr int kAps = C::kSfbAtomsPerStage;
+            int nkb = p.ka - kt * kAps;
+            if (nkb > kAps) nkb = kAps;
             int nrb = p.sfb_rowblocks - tn * (BN / 128);
             if (nrb > BN / 128) nrb = BN / 128;
             const uint32_t db = smem_u32(&sfb_full[s]);
             mbar_arrive_expect_tx(db, static_cast<uint32_t>(nrb * nkb * 512));
             for (int jb = 0; jb < nrb; ++jb)
-              bulk_load(smem_u32(sSfb + s * C::kSfbStageBytes + jb * kKBlocksPerStage * 512),
-                        p.sfb + (static_cast<size_t>(tn * (BN / 128) + jb) * p.ka + kt * kKBlocksPerStage) * 512,
+              bulk_load(smem_u32(sSfb + s * C::kSfbStageBytes + jb * kAps * 512),
+                        p.sfb + (static_cast<size_t>(tn * (BN / 128) + jb) * p.ka + kt * kAps) * 512,
                         static_cast<uint32_t>(nkb * 512), db);
           }
         }
@@ -460,8 +464,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const int f = it - back;
           mbar_wait_drain(smem_u32(&full[f % C::kStages]),
                           static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
-          if (!SP)
-            mbar_wait_drain(smem_u32(&sfb_full[f % C::kStages]),
+          mbar_wait_drain(smem_u32(&sfb_full[f % C::kStages]),
                             static_cast<uint32_t>(f / C::kStages) & 1u, p.err_word);
         }
       }
@@ -587,18 +590,26 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const bool in = m < nm;
             va[m] = in ? __ldg(reinterpret_cast<const uint32_t*>(ga + q * 4 + (kt * 2 + m) * 512)) : 0u;
 #pragma unroll
+            for (int h = 0; h < 2; ++h)
+              vm[2 * m + h] = (in && row < p.M) ? __ldg(reinterpret_cast<const uint32_t*>(gm + 8 * m + 4 * h)) : 0u;
+          }
+          // B scales from the stage's shared-memory copy (see the dense branch).
+          if (!mbar_wait(smem_u32(&sfb_full[s]), static_cast<uint32_t>(it / C::kStages) & 1u,
+                         abort_flag, p.err_word, kErrWaitSfFull)) {
+            ok = false;
+            break;
+          }
+          const uint4* sbs = reinterpret_cast<const uint4*>(sSfb + s * C::kSfbStageBytes);
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+#pragma unroll
             for (int jb = 0; jb < C::kSfbAtoms; ++jb) {
               const int rb = tn * (BN / 128) + jb;
               uint4 x = make_uint4(0u, 0u, 0u, 0u);
-              if (in && rb < p.sfb_rowblocks)
-                x = __ldg(reinterpret_cast<const uint4*>(
-                    p.sfb + (static_cast<size_t>(rb) * p.ka + kt * 2 + m) * 512 + lane * 16));
+              if (m < nm && rb < p.sfb_rowblocks) x = sbs[(jb * 2 + m) * 32 + lane];
               const int o = m * 8 + 4 * jb;
               vb[o + 0] = x.x; vb[o + 1] = x.y; vb[o + 2] = x.z; vb[o + 3] = x.w;
             }
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-              vm[2 * m + h] = (in && row < p.M) ? __ldg(reinterpret_cast<const uint32_t*>(gm + 8 * m + 4 * h)) : 0u;
           }
         } else {
 #pragma unroll
