@@ -181,12 +181,9 @@ __global__ void sparse_compress_kernel(const uint8_t* __restrict__ packed, const
 // row by row (coalesced) into shared memory, then written out as 16 whole 512-byte atoms
 // (coalesced). Rows past `rows` and scales past `ns` are written as zero.
 constexpr int kSfTileAtoms = 16;
-__global__ void __launch_bounds__(256) sf_to_tcgen05_kernel(const uint8_t* __restrict__ scales,
-                                                             int rows, int ns, int ka,
-                                                             uint32_t* __restrict__ out) {
+__device__ __forceinline__ void sf_tile(const uint8_t* __restrict__ scales, int rows, int ns, int ka,
+                                        uint32_t* __restrict__ out, int rb, int a0) {
   __shared__ uint32_t tile[128][kSfTileAtoms + 1];  // [row][atom]: the row's 4 scales of the atom
-  const int rb = blockIdx.y;
-  const int a0 = blockIdx.x * kSfTileAtoms;
   const int s0 = a0 * 4;
   uint8_t* tb = reinterpret_cast<uint8_t*>(&tile[0][0]);
   for (int idx = threadIdx.x; idx < 128 * kSfTileAtoms * 4; idx += blockDim.x) {
@@ -203,6 +200,21 @@ __global__ void __launch_bounds__(256) sf_to_tcgen05_kernel(const uint8_t* __res
     const int r = (wi & 3) * 32 + (wi >> 2);
     out[(static_cast<size_t>(rb) * ka + a0 + a) * 128 + wi] = tile[r][a];
   }
+}
+
+// One block per (128-row block, 16 scale atoms) of one operand (blockIdx.z: 0 = first,
+// 1 = second, so both GEMM operands are reordered in one launch): the 128 x 64 canonical
+// scale bytes are read row by row (coalesced) into shared memory, then written out as 16 whole
+// 512-byte atoms (coalesced). Rows past `rows` and scales past `ns` are written as zero.
+__global__ void __launch_bounds__(256) sf_to_tcgen05_kernel(const uint8_t* __restrict__ s0_, int rows0,
+                                                             uint32_t* __restrict__ out0,
+                                                             const uint8_t* __restrict__ s1_, int rows1,
+                                                             uint32_t* __restrict__ out1, int ns, int ka) {
+  const bool second = blockIdx.z == 1;
+  const int rows = second ? rows1 : rows0;
+  if (static_cast<int>(blockIdx.y) * 128 >= rows) return;
+  sf_tile(second ? s1_ : s0_, rows, ns, ka, second ? out1 : out0, blockIdx.y,
+          blockIdx.x * kSfTileAtoms);
 }
 
 int grid_for(size_t work, int block) {
@@ -359,19 +371,26 @@ bool sparse_compress(const uint8_t* packed, int rows, int K, const uint8_t* meta
 
 bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStream_t s,
                    std::string* err) {
-  if (!scales || !out) { set_err(err, "null pointer"); return false; }
-  if (rows <= 0 || K <= 0 || K % 16 != 0) {
+  return sf_to_tcgen05_pair(scales, rows, nullptr, 0, K, out, nullptr, s, err);
+}
+
+bool sf_to_tcgen05_pair(const uint8_t* a, int rows_a, const uint8_t* b, int rows_b, int K,
+                        uint8_t* out_a, uint8_t* out_b, cudaStream_t s, std::string* err) {
+  if (!a || !out_a || (b && !out_b)) { set_err(err, "null pointer"); return false; }
+  if (rows_a <= 0 || (b && rows_b <= 0) || K <= 0 || K % 16 != 0) {
     set_err(err, "sf_to_tcgen05 needs rows > 0 and K a positive multiple of 16");
     return false;
   }
-  if (reinterpret_cast<uintptr_t>(out) & 3) {
+  if ((reinterpret_cast<uintptr_t>(out_a) | reinterpret_cast<uintptr_t>(out_b)) & 3) {
     set_err(err, "tcgen05 scale output must be 4-byte aligned");
     return false;
   }
   const int ka = (K + 63) / 64;
-  const dim3 grid((ka + kSfTileAtoms - 1) / kSfTileAtoms, (rows + 127) / 128);
-  sf_to_tcgen05_kernel<<<grid, 256, 0, s>>>(scales, rows, K / 16, ka,
-                                            reinterpret_cast<uint32_t*>(out));
+  const int rmax = b && rows_b > rows_a ? rows_b : rows_a;
+  const dim3 grid((ka + kSfTileAtoms - 1) / kSfTileAtoms, (rmax + 127) / 128, b ? 2 : 1);
+  sf_to_tcgen05_kernel<<<grid, 256, 0, s>>>(a, rows_a, reinterpret_cast<uint32_t*>(out_a), b,
+                                            b ? rows_b : 0, reinterpret_cast<uint32_t*>(out_b),
+                                            K / 16, ka);
   return check_launch("sf_to_tcgen05", err);
 }
 

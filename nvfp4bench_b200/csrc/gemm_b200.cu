@@ -1451,8 +1451,7 @@ bool gemm_dense(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err)
     const size_t na = sf_tcgen05_bytes(op.M, op.K), nb = sf_tcgen05_bytes(op.N, op.K);
     uint8_t* ws = scale_workspace(ds, s, na + nb, err);
     if (!ws) return false;
-    if (!sf_to_tcgen05(op.a_scales, op.M, op.K, ws, s, err)) return false;
-    if (!sf_to_tcgen05(op.b_scales, op.N, op.K, ws + na, s, err)) return false;
+    if (!sf_to_tcgen05_pair(op.a_scales, op.M, op.b_scales, op.N, op.K, ws, ws + na, s, err)) return false;
     sfa = ws;
     sfb = ws + na;
     // The weight scales the kernel reads were written by the reorder just enqueued, so the
@@ -1602,8 +1601,7 @@ bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err
     const size_t na = sf_tcgen05_bytes(op.M, vk), nb = sf_tcgen05_bytes(op.N, vk);
     uint8_t* ws = scale_workspace(ds, s, na + nb, err);
     if (!ws) return false;
-    if (!sf_to_tcgen05(op.a_scales, op.M, vk, ws, s, err)) return false;
-    if (!sf_to_tcgen05(op.b_scales, op.N, vk, ws + na, s, err)) return false;
+    if (!sf_to_tcgen05_pair(op.a_scales, op.M, op.b_scales, op.N, vk, ws, ws + na, s, err)) return false;
     sfa = ws;
     sfb = ws + na;
   }

@@ -112,8 +112,8 @@ bool gemm_noalloc(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* er
   }
   uint8_t* scratch = scratch_for_current_device(err);
   if (!scratch) return false;
-  if (!sf_to_tcgen05(op.a_scales, op.M, op.K, scratch, s, err)) return false;
-  if (!sf_to_tcgen05(op.b_scales, op.N, op.K, scratch + na, s, err)) return false;
+  if (!sf_to_tcgen05_pair(op.a_scales, op.M, op.b_scales, op.N, op.K, scratch, scratch + na, s, err))
+    return false;
   return gemm_dense_tc(op, scratch, scratch + na, out, s, err);
 }
 

@@ -51,6 +51,9 @@ bool dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols
                 float global_scale, float* out, cudaStream_t s, std::string* err);
 bool sf_to_tcgen05(const uint8_t* scales, int rows, int K, uint8_t* out, cudaStream_t s,
                    std::string* err);
+// Both GEMM operands' canonical scales reordered in one launch (b may be null: a only).
+bool sf_to_tcgen05_pair(const uint8_t* a, int rows_a, const uint8_t* b, int rows_b, int K,
+                        uint8_t* out_a, uint8_t* out_b, cudaStream_t s, std::string* err);
 // Block size 16 (NVFP4, the reference's codec) or 32 (the scale block of the sparse MMA); the
 // tcgen05 scale layout of block 32 is the block-16 layout of a [rows x cols/2] operand.
 bool quantize_block(const float* src, int rows, int cols, float global_scale, int block,
