@@ -57,3 +57,20 @@ def test_cli_reports_nvml_clocks():
     if "unavailable" not in line[0]:
         mx = int(line[0].split("max ")[1].split(" MHz")[0])
         assert 1000 <= mx <= 3000, line[0]
+
+
+def test_cli_csv_report(tmp_path):
+    """--csv writes the reference's report columns (src/bench.cu:154-164) plus the roofline
+    ones, one row per (kernel, shape, mode)."""
+    import csv
+    out = tmp_path / "r.csv"
+    r = _run(["--kernel", "b200", "--mode", "both", "--m", "512", "--n", "640", "--k", "1024",
+              "--validate", "--iters", "3", "--warmup", "1", "--csv", str(out)])
+    assert r.returncode == 0, r.stdout + r.stderr
+    rows = list(csv.DictReader(out.open()))
+    assert [row["mode"] for row in rows] == ["dense", "2:4"], rows
+    for row in rows:
+        assert row["kernel"] == "b200" and (row["M"], row["N"], row["K"]) == ("512", "640", "1024")
+        assert float(row["sust_tflops"]) > 0 and float(row["min_ms"]) > 0
+        assert row["validated"] == "1" and row["pass"] == "1", row
+        assert float(row["err_over_cinf"]) <= 1e-3  # FP32 output: the GEMM criterion
