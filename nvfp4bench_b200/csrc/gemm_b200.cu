@@ -253,7 +253,9 @@ __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, co
                                             int col0) {
   const int lane = threadIdx.x & 31;
   // A warp's 4 KB staging area holds two BF16 chunks (2 KB each, used in turn) or one FP32 chunk.
-  const bool dbl = p.out_bf16 != 0;
+  // With peer destinations a BF16 warp also stages 64-column pairs there (stage_pair), so every
+  // chunk then waits for all earlier stores to have read the whole area.
+  const bool dbl = p.out_bf16 != 0 && !(kPeers && p.n_peers > 0);
   uint8_t* b = e.buf + (dbl ? (e.count & 1) * 2048 : 0);
   if (lane == 0) {  // the store that last used this buffer has read it
     if (dbl) bulk_wait_group_read<1>();
@@ -291,6 +293,39 @@ __device__ __forceinline__ void stage_chunk(const GemmParams& p, EpiStage& e, co
   ++e.count;
 }
 
+// BF16 output with peer destinations: two adjacent 32-column chunks staged as one 32 x 64 tile
+// (128-byte rows, 128-byte swizzle) and stored with one 64-column box to this GPU's C and to
+// every peer. A 64-byte row per box used about half of an NVLink's bandwidth; 128-byte rows
+// carry FP32 output at about 0.8 of it. The wide maps follow the narrow peer maps in
+// p.peer_maps: [n narrow peers][n wide peers][wide local C].
+__device__ __forceinline__ void stage_pair(const GemmParams& p, EpiStage& e, const uint32_t (&r0)[32],
+                                           const uint32_t (&r1)[32], int col0) {
+  const int lane = threadIdx.x & 31;
+  uint8_t* b = e.buf;
+  if (lane == 0) bulk_wait_group_read<0>();
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t* r = j < 4 ? r0 : r1;
+    const int o = 8 * (j & 3);
+    uint4 w;
+    w.x = pack_bf16x2(__uint_as_float(r[o + 0]) * p.alpha, __uint_as_float(r[o + 1]) * p.alpha);
+    w.y = pack_bf16x2(__uint_as_float(r[o + 2]) * p.alpha, __uint_as_float(r[o + 3]) * p.alpha);
+    w.z = pack_bf16x2(__uint_as_float(r[o + 4]) * p.alpha, __uint_as_float(r[o + 5]) * p.alpha);
+    w.w = pack_bf16x2(__uint_as_float(r[o + 6]) * p.alpha, __uint_as_float(r[o + 7]) * p.alpha);
+    *reinterpret_cast<uint4*>(b + lane * 128 + ((j ^ (lane & 7)) << 4)) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const int n = p.n_peers;
+    tma_store_2d(p.peer_maps + 2 * n, smem_u32(b), col0, e.row0);
+    for (int i = 0; i < n; ++i) tma_store_2d(p.peer_maps + n + i, smem_u32(b), col0, e.row0);
+    bulk_commit_group();
+  }
+  e.count += 2;
+}
+
 // Load CNT chunks of the accumulator with back-to-back tcgen05.ld and one wait, optionally
 // release them (arrive on `early_bar`) as soon as they are in registers, then store them.
 template <int CNT, bool kRemote = false, bool kPeers = true>
@@ -307,6 +342,13 @@ __device__ __forceinline__ void epi_group(const GemmParams& p, EpiStage& e, uint
     if ((threadIdx.x & 31) == 0) {
       if (kRemote) mbar_arrive_cluster(early_bar);
       else mbar_arrive(early_bar);
+    }
+  }
+  if constexpr (kPeers && CNT >= 2) {
+    if (p.out_bf16 && p.tma_store && p.n_peers > 0 && cs[1] == cs[0] + 1) {
+      stage_pair(p, e, r[0], r[1], col_base + cs[0] * 32);
+      if constexpr (CNT == 3) stage_chunk<kPeers>(p, e, r[2], col_base + cs[2] * 32);
+      return;
     }
   }
 #pragma unroll
@@ -1086,7 +1128,7 @@ bool encode_operand_map(CUtensorMap* map, const void* base, int rows, int K, int
 // Row-major output [M][N] (row pitch `pitch` elements) as a 2-D tensor, box 32 x 32 elements, swizzled to match the
 // epilogue's staging layout (64-byte rows for BF16, 128-byte rows for FP32).
 bool encode_output_map(CUtensorMap* map, void* base, int M, int N, long pitch, bool bf16,
-                       std::string* err) {
+                       std::string* err, bool wide = false) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) {
     set_err(err, "cuTensorMapEncodeTiled unavailable from the driver");
@@ -1095,11 +1137,12 @@ bool encode_output_map(CUtensorMap* map, void* base, int M, int N, long pitch, b
   const size_t es = bf16 ? 2 : 4;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch * es)};
-  cuuint32_t box[2] = {32, 32};
+  // wide (BF16 only): box 64 x 32, 128-byte rows, 128-byte swizzle.
+  cuuint32_t box[2] = {wide ? 64u : 32u, 32};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                    base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   (bf16 && !wide) ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_err(err, "cuTensorMapEncodeTiled (output) failed (code " + std::to_string(static_cast<int>(r)) + ")");
@@ -1208,7 +1251,7 @@ DeviceState* device_state(std::string* err) {
 
 // Tensor maps of the peer destinations live in device memory (a kernel parameter would not
 // hold seven of them). One small array per distinct set of destinations and shape, built on
-// first use and kept for the life of the process (at most 896 bytes each): an array handed to
+// first use and kept for the life of the process (at most 1920 bytes each): an array handed to
 // a launch is never freed under it, whichever host thread made the call. Callers that keep
 // making new destination sets (new buffers every call) hit the cap and get an error.
 struct PeerMapsEntry {
@@ -1221,24 +1264,29 @@ struct PeerMapsEntry {
 std::vector<PeerMapsEntry> g_peer_maps;
 constexpr size_t kPeerMapEntries = 4096;
 
-const CUtensorMap* peer_maps(void* const* peers, int n, long rows, long cols, long pitch, int kind,
-                             std::string* err) {
+const CUtensorMap* peer_maps(void* const* peers, int n, const void* local, long rows, long cols,
+                             long pitch, int kind, std::string* err) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     set_err(err, "cudaGetDevice failed");
     return nullptr;
   }
   std::vector<const void*> key(peers, peers + n);
+  key.push_back(local);
   std::lock_guard<std::mutex> lk(g_mu);
   for (const PeerMapsEntry& e : g_peer_maps)
     if (e.dev == dev && e.ptrs == key && e.rows == rows && e.cols == cols && e.pitch == pitch &&
         e.kind == kind)
       return e.d_maps;
-  std::vector<CUtensorMap> maps(n);
-  for (int i = 0; i < n; ++i)
-    if (!encode_output_map(&maps[i], peers[i], static_cast<int>(rows), static_cast<int>(cols), pitch,
-                           kind == 1, err))
+  // FP32: n narrow maps. BF16: n narrow, n wide, then the wide map of the local C.
+  const int count = kind == 1 ? 2 * n + 1 : n;
+  std::vector<CUtensorMap> maps(count);
+  for (int i = 0; i < count; ++i) {
+    void* base = const_cast<void*>(i < 2 * n ? static_cast<const void*>(peers[i % n]) : local);
+    if (!encode_output_map(&maps[i], base, static_cast<int>(rows), static_cast<int>(cols), pitch,
+                           kind == 1, err, i >= n))
       return nullptr;
+  }
   if (g_peer_maps.size() >= kPeerMapEntries) {
     set_err(err, "too many distinct peer destination sets (keep the peer buffers and reuse them)");
     return nullptr;
@@ -1250,8 +1298,8 @@ const CUtensorMap* peer_maps(void* const* peers, int n, long rows, long cols, lo
   ne.cols = cols;
   ne.pitch = pitch;
   ne.kind = kind;
-  if (cudaMalloc(&ne.d_maps, sizeof(CUtensorMap) * n) != cudaSuccess ||
-      cudaMemcpy(ne.d_maps, maps.data(), sizeof(CUtensorMap) * n, cudaMemcpyHostToDevice) !=
+  if (cudaMalloc(&ne.d_maps, sizeof(CUtensorMap) * count) != cudaSuccess ||
+      cudaMemcpy(ne.d_maps, maps.data(), sizeof(CUtensorMap) * count, cudaMemcpyHostToDevice) !=
           cudaSuccess) {
     if (ne.d_maps) cudaFree(ne.d_maps);
     set_err(err, "cudaMalloc/cudaMemcpy of the peer tensor maps failed");
@@ -1299,7 +1347,7 @@ bool setup_output(const Nvfp4DeviceOperands& op, GemmParams& p, void* out, CUten
   const int kind = p.out_bf16 ? 1 : 2;
   if (p.tma_store && !cached_map(MapKey{out, op.M, op.N, 32, kind, ldc}, tc, err)) return false;
   if (op.n_peers > 0) {
-    p.peer_maps = peer_maps(op.d_peers, op.n_peers, op.M, op.N, ldc, kind, err);
+    p.peer_maps = peer_maps(op.d_peers, op.n_peers, out, op.M, op.N, ldc, kind, err);
     if (!p.peer_maps) return false;
     p.n_peers = op.n_peers;
   }
