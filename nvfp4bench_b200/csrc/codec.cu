@@ -8,7 +8,9 @@
 //   dequantize     :99-112
 //   make_random    :115-129 splitmix64 -> uniform [-1, 1)
 // Every float operation is the same IEEE single operation as in the host code (explicit
-// __fdiv_rn / __fmul_rn, no contraction), so bytes match exactly. The linear 128-way scale
+// __fdiv_rn / __fmul_rn, no contraction), so bytes match exactly. The per-element division
+// x / dec feeds only the E2M1 midpoint comparisons, which are made exactly on |x| against
+// per-block thresholds instead (e2m1_quantize_scaled). The linear 128-way scale
 // search becomes a rounding of the float's bits to the UE4M3 grid with ties to the lower code
 // (codec_dev.cuh), which picks the same code: decoded values strictly increase with the code,
 // so the nearest code is one of the two grid points around x, and the errors the reference
@@ -60,9 +62,13 @@ __global__ void quantize_kernel(const float* __restrict__ src, int rows, int col
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int nb = cols / BLK;
   const size_t nblocks = static_cast<size_t>(rows) * nb;
-  for (size_t blk = blockIdx.x * size_t(blockDim.x) + threadIdx.x; blk < nblocks;
-       blk += size_t(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(blk / nb), b = static_cast<int>(blk % nb);
+  const size_t stride = size_t(gridDim.x) * blockDim.x;
+  // (row, block) of the grid-stride index, advanced by the stride's quotient and remainder
+  // instead of a 64-bit division per block.
+  const size_t blk0 = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+  int r = static_cast<int>(blk0 / nb), b = static_cast<int>(blk0 % nb);
+  const int dr = static_cast<int>(stride / nb), db = static_cast<int>(stride % nb);
+  for (size_t blk = blk0; blk < nblocks; blk += stride) {
     const float4* x4 = reinterpret_cast<const float4*>(src + static_cast<size_t>(r) * cols + b * BLK);
     float x[BLK];
 #pragma unroll
@@ -80,14 +86,11 @@ __global__ void quantize_kernel(const float* __restrict__ src, int rows, int col
     const uint8_t sc = e4m3_encode_dev(scale);
     float dec = __fmul_rn(e4m3_decode_dev(sc), g);
     if (dec <= 0.0f) dec = 1.0f;
+    const E2m1Thresholds th = e2m1_thresholds(dec);
+    const bool fast = amax < th.big;
     uint32_t w[BLK / 8];
 #pragma unroll
-    for (int q = 0; q < BLK / 8; ++q) {
-      w[q] = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        w[q] |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[8 * q + j], dec))) << (4 * j);
-    }
+    for (int q = 0; q < BLK / 8; ++q) w[q] = e2m1_pack8(x + 8 * q, dec, th, fast);
     uint8_t* dst = packed + (static_cast<size_t>(r) * cols + b * BLK) / 2;
     if (BLK == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
     else *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[BLK / 8 > 2 ? 2 : 0], w[BLK / 8 > 3 ? 3 : 0]);
@@ -95,6 +98,12 @@ __global__ void quantize_kernel(const float* __restrict__ src, int rows, int col
     if (scales_tc) {
       const size_t atom = static_cast<size_t>(r / 128) * ka + b / 4;
       scales_tc[atom * 512 + (r % 32) * 16 + ((r / 32) % 4) * 4 + (b % 4)] = sc;
+    }
+    r += dr;
+    b += db;
+    if (b >= nb) {
+      b -= nb;
+      ++r;
     }
   }
 }

@@ -74,6 +74,63 @@ __device__ __forceinline__ uint8_t e2m1_quantize_dev(float x) {
   return static_cast<uint8_t>(sign | best);
 }
 
+// e2m1_quantize_dev(x / dec) without the division, for one scale block. With y = |x| / dec
+// exact and every midpoint m having an even float mantissa, the rounded quotient exceeds m
+// exactly when y > m + ulp(m)/2 (a tie rounds back to m), i.e. when |x| > (m + ulp(m)/2) * dec.
+// That product is exact in double (25 + 24 significant bits), and for a float a and a double T,
+// a > T exactly when a > T rounded down to float. So each block takes seven products and roundings
+// and each element seven float compares. The quotient's sign bit survives unless it rounds to
+// zero (|x| / dec <= 2^-150). Quotients from 2^24 up, NaN and infinities take the division path.
+struct E2m1Thresholds {
+  float t[7];   // rounded-down (m + ulp(m)/2) * dec for the midpoints .25 .. 5
+  float big;    // rounded-up 2^24 * dec: the fast path needs |x| below it
+  float zero;   // rounded-down 2^-150 * dec: quotients at or below it round to zero
+};
+__device__ __forceinline__ E2m1Thresholds e2m1_thresholds(float dec) {
+  const double d = static_cast<double>(dec);
+  E2m1Thresholds th;
+  th.t[0] = __double2float_rd((0.25 + 0x1p-26) * d);
+  th.t[1] = __double2float_rd((0.75 + 0x1p-25) * d);
+  th.t[2] = __double2float_rd((1.25 + 0x1p-24) * d);
+  th.t[3] = __double2float_rd((1.75 + 0x1p-24) * d);
+  th.t[4] = __double2float_rd((2.5 + 0x1p-23) * d);
+  th.t[5] = __double2float_rd((3.5 + 0x1p-23) * d);
+  th.t[6] = __double2float_rd((5.0 + 0x1p-22) * d);
+  th.big = __double2float_ru(16777216.0 * d);
+  th.zero = __double2float_rd(0x1p-150 * d);
+  return th;
+}
+// The fast path alone, for |x| < th.big (NaN included: its code is 0, as the division's).
+__device__ __forceinline__ uint32_t e2m1_code_fast(float x, const E2m1Thresholds& th) {
+  const float a = fabsf(x);
+  // The count of thresholds below a, by binary search over the sorted thresholds.
+  const bool h = a > th.t[3];
+  const bool m = a > (h ? th.t[5] : th.t[1]);
+  const bool l = a > (h ? (m ? th.t[6] : th.t[4]) : (m ? th.t[2] : th.t[0]));
+  const uint32_t i = (h ? 4u : 0u) | (m ? 2u : 0u) | (l ? 1u : 0u);
+  return ((x < 0.0f && a > th.zero) ? 0x8u : 0x0u) | i;
+}
+__device__ __forceinline__ uint8_t e2m1_quantize_scaled(float x, float dec, const E2m1Thresholds& th) {
+  if (fabsf(x) < th.big) return static_cast<uint8_t>(e2m1_code_fast(x, th));
+  return e2m1_quantize_dev(__fdiv_rn(x, dec));
+}
+
+// 8 consecutive codes of a block into one word (low nibble = first element). When the block's
+// amax is below th.big every element takes the fast path (amax ignores NaN, which the fast path
+// codes as 0), so the block branches once instead of once per element.
+__device__ __forceinline__ uint32_t e2m1_pack8(const float* x, float dec, const E2m1Thresholds& th,
+                                               bool fast) {
+  uint32_t w = 0;
+  if (fast) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= e2m1_code_fast(x[j], th) << (4 * j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= static_cast<uint32_t>(e2m1_quantize_scaled(x[j], dec, th)) << (4 * j);
+  }
+  return w;
+}
+
 __device__ __forceinline__ float e2m1_decode_dev(uint8_t code) {
   const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
   const float m = mag[code & 7];
@@ -93,12 +150,10 @@ __device__ __forceinline__ uint8_t quantize16_dev(const float (&x)[16], float g,
   const uint8_t sc = e4m3_encode_dev(scale);
   float dec = __fmul_rn(e4m3_decode_dev(sc), g);
   if (dec <= 0.0f) dec = 1.0f;
-  lo = 0;
-  hi = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) lo |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[j], dec))) << (4 * j);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) hi |= static_cast<uint32_t>(e2m1_quantize_dev(__fdiv_rn(x[8 + j], dec))) << (4 * j);
+  const E2m1Thresholds th = e2m1_thresholds(dec);
+  const bool fast = amax < th.big;
+  lo = e2m1_pack8(x, dec, th, fast);
+  hi = e2m1_pack8(x + 8, dec, th, fast);
   return sc;
 }
 

@@ -81,6 +81,9 @@ constexpr int kSfbOff = 16;
 #ifndef NVFP4_SF_SLOTS
 #define NVFP4_SF_SLOTS 2
 #endif
+#ifndef NVFP4_PAIR_SF_SLOTS
+#define NVFP4_PAIR_SF_SLOTS NVFP4_SF_SLOTS
+#endif
 
 // SP: the sparse variant (tcgen05.mma.sp, pair-wise 2:4 A): a stage is 256 logical K, A
 // compressed to 64 bytes per row (one 64-byte-swizzled TMA box), two sparse MMAs of N = BN.
@@ -792,7 +795,7 @@ struct PairCfg {
   static constexpr int kCBytes = 4 * 2 * kCBufBytes;
   static constexpr int kBarBytes = 512;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kCBytes + kBarBytes;
-  static constexpr int kSfSlots = NVFP4_SF_SLOTS;       // ring of per-stage scale slots
+  static constexpr int kSfSlots = NVFP4_PAIR_SF_SLOTS;  // ring of per-stage scale slots
   static constexpr int kSfCol = kTmemCols - kSfSlots * kSfSlotCols;
   static constexpr int kAccBase1 = kSfCol - 256;       // as in the one-SM N=256 kernel
   static constexpr int kOverlapChunks = (256 - kAccBase1 + 31) / 32;
