@@ -1591,12 +1591,13 @@ bool gemm_dense_tc(const Nvfp4DeviceOperands& op, const uint8_t* sfa, const uint
   p.tiles_m = cg == 2 ? (op.M + 255) / 256 : tiles_m;
   p.tiles_n = (op.N + bn - 1) / bn;
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.group_m = 16;
   p.ka = (op.K + 63) / 64;
   p.num_kt = (op.K + 255) / 256;
   p.sfb_rowblocks = (op.N + 127) / 128;
   p.sfa_rowblocks = (op.M + 127) / 128;
-  p.group_m = cg == 2 ? 8 : 16;
+  // Tile raster: groups of group_m tile rows walked down M first, so one band of B is reused by
+  // a whole group while it is in L2 (32 one-SM rows: 1% faster than 16 at C2 and C4, 8 slower).
+  p.group_m = cg == 2 ? 8 : 32;
   p.err_word = ds->err_word;
   if (!setup_nvfp4_out(op, p, s, err)) return false;
   CUtensorMap ta, tb;
@@ -1674,7 +1675,7 @@ bool gemm_sparse(const Nvfp4DeviceOperands& op, cudaStream_t s, std::string* err
   p.tiles_m = (op.M + 127) / 128;
   p.tiles_n = (op.N + 255) / 256;
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.group_m = 16;
+  p.group_m = 32;
   p.ka = (op.K + 127) / 128;          // MMAs (and scale atoms) along K
   p.num_kt = (op.K + 255) / 256;      // 256-K stages
   p.sfb_rowblocks = (op.N + 127) / 128;
