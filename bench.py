@@ -24,7 +24,8 @@ counts the headline's timed region only.
 `value` is device-timed with operands resident in HBM: for M > 128 the L2 is flushed (256 MiB
 write) before every step and CUDA events bracket each launch; decode shapes rotate the weight
 over copies larger than 3x L2 and time the K back-to-back steps with one event pair (the next
-launch's prologue overlaps through programmatic dependent launch); max over ranks.
+launch's prologue overlaps through programmatic dependent launch); max over ranks. Decode
+shapes are also timed as replays of one captured CUDA graph of >= 100 launches (`graph`).
 --quantize-a adds the GPU quantisation of fp32 A to every (decode) step. `e2e` is the same
 metric through the C ABI with pinned host buffers: each step copies the quantised operands
 host->device, launches, and copies C device->host, all inside the timed region (consecutive
@@ -224,6 +225,34 @@ EXTRA_CONFIGS = ("c1", "c2-canonical", "c3", "c4", "decode-up-16", "decode-up-64
                  "decode-down-16", "decode-down-64", "decode-down-128")
 
 
+def graph_ms_per_launch(api, rot, stream, dev, replays=3):
+    """Per-launch time of a captured CUDA graph of >= 100 launches over the argument blocks
+    `rot` (the rotated weight copies; programmatic dependent launch edges between them),
+    replayed `replays` times between one event pair on `stream`. Returns (ms, launches)."""
+    import torch
+    n_launch = -(-100 // len(rot)) * len(rot)
+    g = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(g, stream=cap):
+            for i in range(n_launch):
+                api.launch(rot[i % len(rot)])
+    stream.wait_stream(cap)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(100_000)
+    e0.record(stream)
+    for _ in range(replays):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (replays * n_launch)
+    del g
+    return ms, n_launch
+
+
 def time_extra(api, name, dev, steps, ladder, hbm_gbs):
     """Operands for workload `name` made and quantised on the GPU, then `steps` timed steps
     under the headline's rules: M > 128 flushes L2 (256 MiB write) before each step and times
@@ -299,6 +328,7 @@ def time_extra(api, name, dev, steps, ladder, hbm_gbs):
             e_.record(stream)
         torch.cuda.synchronize()
         ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / steps
+    g_ms = graph_ms_per_launch(api, rot, stream, dev)[0] if decode else None
     if api.device_error():
         raise RuntimeError(f"{name}: device error word set")
     flops = 2.0 * M * N * K
@@ -312,6 +342,9 @@ def time_extra(api, name, dev, steps, ladder, hbm_gbs):
     if decode:
         r["roofline"] = {"bound": "hbm", "peak": hbm_gbs, "unit": "GB/s",
                          "frac": r["gbs"] / hbm_gbs, "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+        # The same launches replayed from one CUDA graph (>= 100 per replay).
+        r["graph"] = {"ms_per_step": g_ms, "gbs": abytes / (g_ms * 1e-3) / 1e9,
+                      "frac": abytes / (g_ms * 1e-3) / 1e9 / hbm_gbs}
     else:
         key = "sparse_random_burst" if sparse else "random_burst"
         peak = (ladder.get(key) or {}).get("tflops")
@@ -491,14 +524,31 @@ def run_b200(args, rank, world, local_rank):
     if derr:
         raise RuntimeError(f"device error word {derr:#x}")
 
+    # Decode shapes again from one captured CUDA graph: >= 100 launches over the rotated weight
+    # copies (programmatic dependent launch edges between them), replayed three times between
+    # one event pair - the form a serving loop would use. Reported beside the stream timing.
+    graph = None
+    if decode and xa is None:
+        if world > 1:
+            dist.barrier()
+        g_ms, n_launch = graph_ms_per_launch(api, rot, stream, dev)
+        g_ms = max_over_ranks([g_ms], device=dev)[0]
+        derr = api.device_error()
+        if derr:
+            raise RuntimeError(f"device error word {derr:#x} (graph replay)")
+        graph = {"ms_per_step": g_ms, "launches_per_replay": n_launch, "replays": 3,
+                 "value": world * 2.0 * M * N * K / (g_ms * 1e-3) / 1e12}
+
     flops = 2.0 * M * N * K
     value = world * flops / (mean_ms * 1e-3) / 1e12
     achieved = flops / (mean_ms * 1e-3) / 1e12
     if args.kernel_only:
         if rank == 0:
-            print(json.dumps({"metric": "nvfp4_gemm_tflops", "value": value, "unit": "TFLOP/s",
-                              "ms_per_step": mean_ms, "kernel_only": True,
-                              "config": {"workload": desc}}), flush=True)
+            line = {"metric": "nvfp4_gemm_tflops", "value": value, "unit": "TFLOP/s",
+                    "ms_per_step": mean_ms, "kernel_only": True, "config": {"workload": desc}}
+            if graph:
+                line["graph"] = graph
+            print(json.dumps(line), flush=True)
         return 0
 
     # Reference-style timing (src/bench.cu:90-105): per-launch events, no flush, burst=min,
@@ -723,6 +773,8 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": args.steps * (2 if args.quantize_a and not fused_qa else 1),
         "clocks": clk,
     }
+    if graph is not None:
+        line["graph"] = graph
     if gather is not None:
         line["gather"] = gather
     if world == 1 and not args.no_extras:
