@@ -336,7 +336,7 @@ def time_extra(api, name, dev, steps, ladder, hbm_gbs):
     r = {"workload": desc + (" (canonical scales, reordered every call)" if canonical else ""),
          "M": M, "N": N, "K": K, "ms_per_step": ms, "tflops": flops / (ms * 1e-3) / 1e12,
          "gbs": abytes / (ms * 1e-3) / 1e9, "algorithmic_bytes": abytes,
-         "gpu_launches_per_step": 3 if canonical else 1,
+         "gpu_launches_per_step": 2 if canonical else 1,
          "l2": ("weight rotated over %d copies (> 3x L2)" % len(rot)) if decode else
                "flushed before every step"}
     if decode:

@@ -194,6 +194,26 @@ __device__ __forceinline__ void sf_tile(const uint8_t* __restrict__ scales, int 
                                         uint32_t* __restrict__ out, int rb, int a0) {
   __shared__ uint32_t tile[128][kSfTileAtoms + 1];  // [row][atom]: the row's 4 scales of the atom
   const int s0 = a0 * 4;
+  if ((ns & 3) == 0 && (reinterpret_cast<uintptr_t>(scales) & 3) == 0) {
+    // Whole rows of 4-scale words (K a multiple of 64): one word per (row, atom), all of a
+    // thread's loads issued before any is stored, so the block waits on memory once.
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(scales);
+    constexpr int kWords = 128 * kSfTileAtoms;
+    constexpr int kPer = kWords / 256;
+    uint32_t v[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int idx = threadIdx.x + i * 256;
+      const int r = idx / kSfTileAtoms, a = idx % kSfTileAtoms;
+      const int row = rb * 128 + r;
+      v[i] = (row < rows && a0 + a < ka) ? s32[static_cast<size_t>(row) * ka + a0 + a] : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int idx = threadIdx.x + i * 256;
+      tile[idx / kSfTileAtoms][idx % kSfTileAtoms] = v[i];
+    }
+  } else {
   uint8_t* tb = reinterpret_cast<uint8_t*>(&tile[0][0]);
   for (int idx = threadIdx.x; idx < 128 * kSfTileAtoms * 4; idx += blockDim.x) {
     const int r = idx / (kSfTileAtoms * 4), c = idx % (kSfTileAtoms * 4);
@@ -201,6 +221,7 @@ __device__ __forceinline__ void sf_tile(const uint8_t* __restrict__ scales, int 
     uint8_t v = 0;
     if (row < rows && sc < ns) v = scales[static_cast<size_t>(row) * ns + sc];
     tb[(r * (kSfTileAtoms + 1) + c / 4) * 4 + (c & 3)] = v;
+  }
   }
   __syncthreads();
   for (int w = threadIdx.x; w < kSfTileAtoms * 128; w += blockDim.x) {
@@ -219,6 +240,10 @@ __global__ void __launch_bounds__(256) sf_to_tcgen05_kernel(const uint8_t* __res
                                                              uint32_t* __restrict__ out0,
                                                              const uint8_t* __restrict__ s1_, int rows1,
                                                              uint32_t* __restrict__ out1, int ns, int ka) {
+  // The GEMM that reads the reordered scales is launched with programmatic stream
+  // serialization and waits for this grid to complete before reading them; letting it launch
+  // now overlaps its set-up with this kernel.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const bool second = blockIdx.z == 1;
   const int rows = second ? rows1 : rows0;
   if (static_cast<int>(blockIdx.y) * 128 >= rows) return;

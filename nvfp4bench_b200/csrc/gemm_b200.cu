@@ -461,6 +461,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization: the set-up above (barriers, TMEM,
+  // descriptor prefetch) overlaps the tail of the previous kernel on the stream, typically the
+  // scale reorder or the quantiser that wrote this GEMM's operands. No thread touches global
+  // memory before that kernel has completed and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -1373,8 +1378,18 @@ bool launch_dense_as(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
     ds->attr_set[idx] = true;
   }
   int grid = p.num_tiles < ds->sms ? p.num_tiles : ds->sms;
-  gemm_mxf4nvf4_kernel<BN, SP, PEERS><<<grid, kNumThreads, C::kSmemBytes, s>>>(ta, tb, tc, p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_mxf4nvf4_kernel<BN, SP, PEERS>, ta, tb, tc, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_err(err, std::string("gemm launch: ") + cudaGetErrorString(e));
     return false;
