@@ -83,10 +83,17 @@ def test_e4m3_boundaries(api, orc):
 
 
 def test_sf_relayout_matches_oracle(api, orc):
-    for rows, K in ((128, 256), (300, 320), (1, 16), (1000, 4096)):
+    # Word-wide loads when K % 64 == 0 and the source is 4-byte aligned (1088: a partial second
+    # tile of 16 atoms), byte loads otherwise (K = 16, 1040, and a source one byte off).
+    for rows, K in ((128, 256), (300, 320), (1, 16), (1000, 4096), (129, 1088), (257, 1040)):
         s = torch.randint(0, 256, (rows, K // 16), dtype=torch.uint8, device="cuda")
         got = api.sf_to_tcgen05(s, rows, K).cpu().numpy()
         assert np.array_equal(got, orc.sf_to_tcgen05(s.cpu().numpy(), K))
+    rows, K = 200, 512
+    flat = torch.randint(0, 256, (rows * (K // 16) + 1,), dtype=torch.uint8, device="cuda")
+    s = flat[1:].view(rows, K // 16)
+    got = api.sf_to_tcgen05(s, rows, K).cpu().numpy()
+    assert np.array_equal(got, orc.sf_to_tcgen05(s.cpu().numpy(), K))
 
 
 def test_quantize_rejects_bad_shape(api):
