@@ -617,6 +617,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int tm, tn;
       tile_coords(p, t, tm, tn);
       const uint8_t* ga = p.sfa + static_cast<size_t>(tm) * p.ka * 512 + lane * 16;
+      if (wgroup == 0) {
+        // The tile's A scale atoms (ka x 512 bytes) into L2 at once, quadrant q taking every
+        // fourth 128-byte line, so that the per-stage loads below wait for L2, not DRAM, on
+        // the first tiles after the operands were written or evicted.
+        const uint8_t* row_block = p.sfa + static_cast<size_t>(tm) * p.ka * 512;
+        for (int l = q * 32 + lane; l < p.ka * 4; l += 128)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(row_block + static_cast<size_t>(l) * 128));
+      }
       for (int kt = 0; kt < p.num_kt && ok; ++kt, ++it) {
         if ((it % kWriterGroups) != wgroup) continue;
         const int s = it % C::kStages;
